@@ -1,0 +1,197 @@
+/*
+ * ie_tpq.h -- C ABI of libie_tpq.so, the B200 (sm_100a) tensor-parallel
+ * quantized linear path.
+ *
+ * This is the drop-in boundary for the reference engine's column-/row-parallel
+ * Linear layers (ie/parallel/sharding.py) combined with its int8 / int4 / fp8
+ * weight formats (ie/quant/).  Everything crossing it is a plain pointer, an
+ * integer or a POD struct: no C++ or torch types.  Device pointers are raw
+ * CUDA addresses; `stream` is a cudaStream_t passed as void*.
+ *
+ * Conventions
+ *   - Every entry point returns IE_OK (0) or an error code; the message of the
+ *     last failure on the calling thread is available from ie_last_error().
+ *   - Nothing synchronises the host: work is enqueued on the caller's stream.
+ *   - The caller owns inputs, outputs and workspace.  The library owns only
+ *     what ie_comm_create() allocates (landing buffers, flags, status word).
+ *   - Weight layout of the reference: W is [K_in, N_out] and y = x @ W
+ *     (ie/model/transformer.py:48-61).  Packed device layouts are K-contiguous
+ *     per output row ([N, K]) so that the weight streams row by row.
+ */
+#ifndef IE_TPQ_H
+#define IE_TPQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IE_TPQ_ABI_VERSION 1
+
+/* ---- status codes --------------------------------------------------- */
+#define IE_OK 0
+#define IE_ERR_INVALID 1     /* bad shape / format / alignment / rank: Python raises ValueError */
+#define IE_ERR_CUDA 2        /* a CUDA runtime call failed: RuntimeError */
+#define IE_ERR_TIMEOUT 3     /* a bounded wait on a peer ran out (device status word) */
+#define IE_ERR_UNSUPPORTED 4 /* valid request this build does not implement */
+
+/* ---- enums ------------------------------------------------------------ */
+/* weight formats (ie/quant/formats.py:67-71 and the group-128 int4 scheme) */
+#define IE_FMT_INT8 0        /* int8 codes in [-127, 127], symmetric (INT8) */
+#define IE_FMT_INT4 1        /* 4-bit codes: asym [0,15] with zeros, or sym [-7,7] stored +8 */
+#define IE_FMT_FP8_E4M3 2    /* e4m3 bytes of the reference's f32 codes (FP8_E4M3) */
+
+/* where the scale sits.  The reference's axis argument is the KEPT dimension
+ * of the [K, N] weight (ie/quant/weights.py:45-48): PER_OUTPUT_CHANNEL = 0
+ * keeps K, i.e. one scale per input row. */
+#define IE_AXIS_K 0          /* f32 scale[K]        (reference axis=0, its default) */
+#define IE_AXIS_N 1          /* f32 scale[N]        (reference axis=1)              */
+#define IE_AXIS_TENSOR 2     /* f32 scale[1]        (reference axis=None)           */
+#define IE_AXIS_GROUP128 3   /* f16 scale[N][K/128] and f16 zero[N][K/128]          */
+
+/* element types */
+#define IE_DT_BF16 0
+#define IE_DT_F16 1
+#define IE_DT_F32 2
+#define IE_DT_I32 3
+#define IE_DT_U8 4
+
+/* epilogue flags for ie_qlinear / ie_qlinear_allreduce */
+#define IE_EPI_BIAS 1        /* out += bias[n] (f32), added once after any reduction */
+#define IE_EPI_RESIDUAL 2    /* out = residual + (...), residual has out's dtype      */
+#define IE_EPI_SILU_MUL 4    /* rows are gate/up pairs: out[:, j] = silu(row 2j) * row 2j+1 */
+
+/* ---- packed weight ------------------------------------------------------ */
+typedef struct ie_qweight {
+  int32_t format;       /* IE_FMT_* */
+  int32_t axis;         /* IE_AXIS_* */
+  int64_t k;            /* contraction length (reference rows of W) */
+  int64_t n;            /* packed rows (reference columns of W; 2x for gate/up pairs) */
+  const void* codes;    /* INT8/FP8: [n][k] bytes.  INT4: [n][k/2] bytes; each 32-bit word
+                           holds k0..k0+7 with nibble p = code of k0 + {0,2,4,6,1,3,5,7}[p] */
+  const void* scale;    /* per axis above; for gate/up pairs with IE_AXIS_K: f32 [2][k]
+                           (gate table then up table) */
+  const void* zero;     /* f16 [n][k/128] for IE_AXIS_GROUP128, else NULL */
+  int32_t int4_symmetric; /* INT4 only: 1 = codes stored as q+8 with an implicit zero of 8 */
+  int32_t gate_up;        /* 1 = rows interleaved gate/up (use with IE_EPI_SILU_MUL) */
+} ie_qweight;
+
+/* ---- one linear layer --------------------------------------------------- */
+typedef struct ie_qlinear_args {
+  ie_qweight w;
+  int64_t m;            /* tokens */
+  int32_t act_dtype;    /* x dtype: IE_DT_BF16 / IE_DT_F16 / IE_DT_F32 */
+  int32_t out_dtype;    /* out dtype: IE_DT_BF16 / IE_DT_F16 / IE_DT_F32 */
+  const void* x;        /* [m][k] row stride ldx (elements) */
+  int64_t ldx;
+  void* out;            /* [m][n] (or [m][n/2] with SILU_MUL), row stride ldo */
+  int64_t ldo;
+  const float* bias;    /* [n] f32 or NULL */
+  const void* residual; /* [m][n] of out_dtype, row stride ldr, or NULL */
+  int64_t ldr;
+  int32_t epilogue;     /* IE_EPI_* flags */
+  int32_t algo;         /* 0 = auto; 1 = weight-streaming GEMV; 2 = tcgen05 tensor-core GEMM */
+  void* workspace;      /* caller-owned scratch (see ie_qlinear_workspace_size), may be NULL */
+  size_t workspace_bytes;
+} ie_qlinear_args;
+
+/* ---- library ------------------------------------------------------------ */
+int ie_version(void);
+/* Copy the last error message of this thread into buf (NUL-terminated). */
+int ie_last_error(char* buf, size_t n);
+
+/* ---- quantizer (reference semantics, bit-exact) ----------------------------
+ * Replaces ie/quant/weights.py:51-70 (quantize_integer) and :73-81
+ * (quantize_float) for a 2-D f32 weight w[rows][cols] in device memory.
+ * axis: 0 keeps rows (one scale per row), 1 keeps columns, -1 = per tensor.
+ *   integer (fmt_bits 8 or 4): codes int32 [rows][cols]; symmetric -> zero NULL;
+ *     asymmetric -> zero f32, same shape as scale.
+ *   float (IE_FMT_FP8_E4M3 via ie_quantize_float): codes f32 [rows][cols].
+ * scale/zero hold rows (axis 0), cols (axis 1) or 1 (axis -1) f32 values. */
+int ie_quantize_integer(const float* w, int64_t rows, int64_t cols, int32_t bits,
+                        int32_t symmetric, int32_t axis, int32_t* codes, float* scale,
+                        float* zero, void* stream);
+/* exponent/mantissa bits and reserves_infinity as in ie/quant/formats.py:34-64 */
+int ie_quantize_float(const float* w, int64_t rows, int64_t cols, int32_t exponent_bits,
+                      int32_t mantissa_bits, int32_t reserves_infinity, int32_t axis,
+                      float* codes, float* scale, void* stream);
+/* Replaces ie/quant/formats.py:74-79 (round_to_float_format), elementwise. */
+int ie_round_to_float_format(const float* x, float* out, int64_t count, int32_t exponent_bits,
+                             int32_t mantissa_bits, int32_t reserves_infinity, void* stream);
+
+/* ---- packing: reference tables -> device layout ------------------------------
+ * Replaces nothing in the reference (it keeps f32 fake-quant weights,
+ * ie/quant/model.py:48-52); this is the step that makes the weights real.
+ * codes_kn: the reference's codes, [k][n] (int32 for INT8/INT4, f32 for FP8).
+ * For IE_AXIS_GROUP128 pass codes_nk [n][k] int32 (the group view of
+ * ie/quant/weights.py:51-70 on W.T), scale_f32/zero_f32 [n][k/128].
+ * Outputs: packed codes in out_codes, f16 tables for GROUP128 in out_scale16 /
+ * out_zero16.  *unrepresentable (device int32, may be NULL) counts FP8 codes
+ * that e4m3 cannot hold and were rounded to the nearest e4m3 value. */
+int ie_pack_weight(int32_t format, int32_t axis, int32_t int4_symmetric, int64_t k, int64_t n,
+                   const void* codes, const float* scale_f32, const float* zero_f32,
+                   void* out_codes, void* out_scale16, void* out_zero16,
+                   int32_t* unrepresentable, void* stream);
+/* Packed -> dense reference-equivalent weight.  layout 0: f32 [k][n]
+ * (ie/quant/weights.py:22-26); layout 1: out_dtype [n][k] (for cuBLAS). */
+int ie_dequantize(const ie_qweight* w, int32_t layout, int32_t out_dtype, void* out,
+                  void* stream);
+
+/* ---- single-rank quantized linear --------------------------------------------
+ * Replaces ColumnParallelLinear.forward / RowParallelLinear.forward
+ * (ie/parallel/sharding.py:51-66) and the projections of TorchBlock.forward
+ * (ie/model/torch_transformer.py:36-38,60) and torch_backend.swiglu
+ * (ie/kernels/torch_backend.py:125-127) on a packed shard. */
+size_t ie_qlinear_workspace_size(const ie_qlinear_args* a);
+int ie_qlinear(const ie_qlinear_args* a, void* stream);
+
+/* ---- RMSNorm ------------------------------------------------------------------
+ * Replaces ie/layers/functional.py:6-8 (rms_norm) and
+ * ie/kernels/torch_backend.py:103-105: out = x / sqrt(mean(x^2) + eps) * weight
+ * per row of x [m][h], f32 arithmetic; weight is f32 [h]. */
+int ie_rms_norm(const void* x, int64_t ldx, int32_t x_dtype, const float* weight, void* out,
+                int64_t ldo, int32_t out_dtype, int64_t m, int64_t h, float eps, void* stream);
+
+/* ---- all_reduce over a list of partials in one process -----------------------
+ * Replaces ie/parallel/sharding.py:40-44: out = p[0] + p[1] + ... in rank order
+ * (f32 arithmetic, the reference's order).  dtype applies to inputs and out. */
+int ie_reduce_partials(const void* const* partials, int32_t count, void* out, int64_t numel,
+                       int32_t dtype, void* stream);
+
+/* ---- tensor-parallel communicator (one process per GPU) ------------------------
+ * The reference's all_reduce runs ranks as list entries in one process
+ * (ie/parallel/tensor_parallel.py:68-73); here each rank is a process on its
+ * own GPU and peers reach each other's landing buffers over NVLink through
+ * CUDA IPC.  Sequence: ie_comm_create -> ie_comm_export (bytes to all-gather
+ * between ranks) -> ie_comm_open -> any number of collectives -> ie_comm_destroy. */
+typedef struct ie_comm ie_comm;
+#define IE_COMM_HANDLE_BYTES 64
+int ie_comm_create(int32_t rank, int32_t world, int32_t device, size_t max_bytes,
+                   ie_comm** out);
+/* writes IE_COMM_HANDLE_BYTES bytes describing this rank's landing buffer */
+int ie_comm_export(ie_comm* c, void* handle_out);
+/* handles: world * IE_COMM_HANDLE_BYTES bytes, rank order */
+int ie_comm_open(ie_comm* c, const void* handles);
+int ie_comm_destroy(ie_comm* c);
+/* bounded-wait limit in nanoseconds for every peer wait (default 2e9) */
+int ie_comm_set_timeout(ie_comm* c, uint64_t ns);
+/* IE_OK, or IE_ERR_TIMEOUT if a kernel of this comm gave up waiting; the
+ * status word is read with a synchronous copy and then cleared. */
+int ie_comm_check(ie_comm* c);
+
+/* Fused row-parallel linear + all-reduce for this rank: every rank calls it with
+ * its own K-shard (ie/parallel/sharding.py:60-66) and gets the reduced
+ * out = [residual +] sum_r x_r @ W_r [+ bias] (ie/parallel/tensor_parallel.py:70,73).
+ * Partials cross NVLink as f32 with P2P stores from the GEMM epilogue and are
+ * summed in rank order, so every rank's output is bitwise identical. */
+int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* stream);
+/* Standalone all-reduce of a device tensor (same one-shot P2P protocol). */
+int ie_allreduce(ie_comm* c, const void* in, void* out, int64_t numel, int32_t dtype,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* IE_TPQ_H */

@@ -1,0 +1,151 @@
+// extern "C" entry points of libie_tpq.so that are not tied to one kernel
+// family: version, error reporting, argument validation and dispatch of the
+// quantized linear layer (single-rank and fused with the all-reduce), and the
+// in-process reduction of a list of partials.
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace ie {
+
+namespace {
+thread_local char g_err[512] = "";
+}
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+const char* last_error() { return g_err; }
+
+namespace {
+
+int validate_linear(const ie_qlinear_args& a) {
+  int rc = validate_qweight(a.w);
+  if (rc) return rc;
+  IE_CHECK(a.m >= 0, "qlinear: negative token count");
+  IE_CHECK(a.act_dtype == IE_DT_BF16 || a.act_dtype == IE_DT_F16 || a.act_dtype == IE_DT_F32,
+           "qlinear: unsupported activation dtype %d", a.act_dtype);
+  IE_CHECK(a.out_dtype == IE_DT_BF16 || a.out_dtype == IE_DT_F16 || a.out_dtype == IE_DT_F32,
+           "qlinear: unsupported output dtype %d", a.out_dtype);
+  if (a.m == 0) return IE_OK;
+  IE_CHECK(a.x && a.out, "qlinear: null x or out");
+  IE_CHECK(a.ldx >= a.w.k, "qlinear: ldx %lld < K %lld", (long long)a.ldx, (long long)a.w.k);
+  const int64_t ncols = (a.epilogue & IE_EPI_SILU_MUL) ? a.w.n / 2 : a.w.n;
+  IE_CHECK(a.ldo >= ncols, "qlinear: ldo %lld < output columns %lld", (long long)a.ldo,
+           (long long)ncols);
+  if (a.epilogue & IE_EPI_SILU_MUL)
+    IE_CHECK(a.w.gate_up, "qlinear: SILU_MUL needs a weight packed as gate/up row pairs");
+  if (a.epilogue & IE_EPI_BIAS) IE_CHECK(a.bias, "qlinear: BIAS flag without a bias pointer");
+  if (a.epilogue & IE_EPI_RESIDUAL) {
+    IE_CHECK(a.residual, "qlinear: RESIDUAL flag without a residual pointer");
+    IE_CHECK(a.ldr >= ncols, "qlinear: ldr %lld < output columns", (long long)a.ldr);
+  }
+  IE_CHECK((a.epilogue & ~(IE_EPI_BIAS | IE_EPI_RESIDUAL | IE_EPI_SILU_MUL)) == 0,
+           "qlinear: unknown epilogue flags 0x%x", a.epilogue);
+  IE_CHECK(a.algo >= 0 && a.algo <= 2, "qlinear: unknown algo %d", a.algo);
+  return IE_OK;
+}
+
+}  // namespace
+}  // namespace ie
+
+using namespace ie;
+
+extern "C" int ie_version(void) { return IE_TPQ_ABI_VERSION; }
+
+extern "C" int ie_last_error(char* buf, size_t n) {
+  if (!buf || n == 0) return IE_ERR_INVALID;
+  std::strncpy(buf, last_error(), n - 1);
+  buf[n - 1] = '\0';
+  return IE_OK;
+}
+
+extern "C" size_t ie_qlinear_workspace_size(const ie_qlinear_args* a) {
+  (void)a;
+  return 0;
+}
+
+extern "C" int ie_qlinear(const ie_qlinear_args* a, void* stream) {
+  IE_CHECK(a, "qlinear: null args");
+  int rc = validate_linear(*a);
+  if (rc || a->m == 0) return rc;
+  IE_CHECK(a->algo != 2, "qlinear: the tensor-core path is not built into this library");
+  return launch_qlinear_gemv(*a, nullptr, 0, as_stream(stream));
+}
+
+extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* stream) {
+  IE_CHECK(c && a, "qlinear_allreduce: null pointer");
+  int rc = validate_linear(*a);
+  if (rc || a->m == 0) return rc;
+  IE_CHECK(!(a->epilogue & IE_EPI_SILU_MUL),
+           "qlinear_allreduce: SILU_MUL belongs to the column-parallel gate/up layer");
+  IE_CHECK(!a->w.gate_up, "qlinear_allreduce: gate/up pairs are column-parallel");
+  IE_CHECK(a->algo != 2, "qlinear_allreduce: the tensor-core path is not built into this library");
+  int resident = 0;
+  rc = gemv_resident_ctas(*a, &resident);
+  if (rc) return rc;
+  IE_CHECK(resident > 0, "qlinear_allreduce: kernel cannot be resident on this device");
+  ReduceCtx ctx;
+  rc = comm_context(c, &ctx, gemv_tiles(*a), a->m * a->w.n);
+  if (rc) return rc;
+  return launch_qlinear_gemv(*a, &ctx, resident, as_stream(stream));
+}
+
+namespace ie {
+namespace reduce_detail {
+
+constexpr int kMaxPartials = 64;
+struct PartialList {
+  const void* p[kMaxPartials];
+};
+
+template <typename T>
+__global__ void reduce_partials_kernel(PartialList pl, int count, T* __restrict__ out,
+                                       int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float v = to_f32<T>(static_cast<const T*>(pl.p[0])[i]);
+    for (int r = 1; r < count; ++r) v += to_f32<T>(static_cast<const T*>(pl.p[r])[i]);
+    out[i] = from_f32<T>(v);
+  }
+}
+
+}  // namespace reduce_detail
+}  // namespace ie
+
+using namespace ie::reduce_detail;
+
+extern "C" int ie_reduce_partials(const void* const* partials, int32_t count, void* out,
+                                  int64_t numel, int32_t dtype, void* stream) {
+  IE_CHECK(partials && out, "reduce_partials: null pointer");
+  IE_CHECK(count >= 1 && count <= kMaxPartials, "reduce_partials: %d partials outside [1, %d]",
+           count, kMaxPartials);
+  IE_CHECK(numel >= 0, "reduce_partials: negative size");
+  if (numel == 0) return IE_OK;
+  PartialList pl{};
+  for (int i = 0; i < count; ++i) {
+    IE_CHECK(partials[i], "reduce_partials: partial %d is null", i);
+    pl.p[i] = partials[i];
+  }
+  cudaStream_t s = as_stream(stream);
+  const int threads = 256;
+  const int grid = (int)std::min<int64_t>((numel + threads * 4 - 1) / (threads * 4), 148 * 16);
+  if (dtype == IE_DT_F32)
+    reduce_partials_kernel<float><<<grid, threads, 0, s>>>(pl, count, static_cast<float*>(out),
+                                                           numel);
+  else if (dtype == IE_DT_BF16)
+    reduce_partials_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
+        pl, count, static_cast<__nv_bfloat16*>(out), numel);
+  else if (dtype == IE_DT_F16)
+    reduce_partials_kernel<__half><<<grid, threads, 0, s>>>(pl, count, static_cast<__half*>(out),
+                                                            numel);
+  else
+    return set_error(IE_ERR_INVALID, "reduce_partials: unsupported dtype %d", dtype);
+  return launch_status("reduce_partials_kernel");
+}

@@ -1,0 +1,79 @@
+"""The quantized linear call: one packed shard times a token batch on the GPU,
+with the epilogue fused in and, for a row-parallel layer, the all-reduce fused
+in as well (``comm=``).  This is the device form of the reference's
+``x @ W_shard`` (ie/parallel/sharding.py:51-66) and of the projections in
+``TorchBlock.forward`` (ie/model/torch_transformer.py:36-38,60) and
+``torch_backend.swiglu`` (ie/kernels/torch_backend.py:125-127).
+"""
+from __future__ import annotations
+
+import ctypes
+
+from . import _lib
+from .device import dtype_code, require_cuda
+from .packed import PackedWeight
+
+ALGO_AUTO, ALGO_GEMV, ALGO_TCGEN05 = 0, 1, 2
+
+
+def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=False,
+               algo=ALGO_AUTO, workspace=None) -> _lib.QLinearArgs:
+    if x.dim() != 2:
+        raise ValueError(f"x must be 2-D [tokens, K], got shape {tuple(x.shape)}")
+    if x.shape[1] != w.k:
+        raise ValueError(f"x has K={x.shape[1]} but the weight has K={w.k}")
+    if x.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("x and out must be contiguous along their last dimension")
+    epi = 0
+    if bias is not None:
+        epi |= _lib.IE_EPI_BIAS
+    if residual is not None:
+        epi |= _lib.IE_EPI_RESIDUAL
+        if residual.dtype != out.dtype or residual.stride(1) != 1:
+            raise ValueError("residual must match out's dtype and be row-contiguous")
+    if silu_mul:
+        epi |= _lib.IE_EPI_SILU_MUL
+    a = _lib.QLinearArgs()
+    a.w = w.qweight()
+    a.m = x.shape[0]
+    a.act_dtype = dtype_code(x.dtype)
+    a.out_dtype = dtype_code(out.dtype)
+    a.x = x.data_ptr()
+    a.ldx = x.stride(0)
+    a.out = out.data_ptr()
+    a.ldo = out.stride(0)
+    a.bias = bias.data_ptr() if bias is not None else None
+    a.residual = residual.data_ptr() if residual is not None else None
+    a.ldr = residual.stride(0) if residual is not None else 0
+    a.epilogue = epi
+    a.algo = algo
+    a.workspace = workspace.data_ptr() if workspace is not None else None
+    a.workspace_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    return a
+
+
+def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | None = None,
+            out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None):
+    """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce.
+
+    x: CUDA tensor ``[M, K]`` (bf16 / f16 / f32).  bias: f32 ``[N]``.  residual:
+    ``[M, N]`` of the output dtype, added after the reduction.  A gate/up pair
+    weight returns ``silu(gate) * up`` of shape ``[M, N/2]``.
+    """
+    torch = require_cuda()
+    if silu_mul is None:
+        silu_mul = w.gate_up
+    out_dtype = out_dtype or x.dtype
+    cols = w.out_features if silu_mul else w.n
+    if out is None:
+        out = torch.empty((x.shape[0], cols), dtype=out_dtype, device=x.device)
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        bias = bias.to(torch.float32).contiguous()
+    a = build_args(x, w, out, bias=bias, residual=residual, silu_mul=silu_mul, algo=algo)
+    s = _lib.stream_ptr(stream)
+    if comm is None:
+        _lib.check(_lib.lib().ie_qlinear(ctypes.byref(a), s), "qlinear")
+    else:
+        _lib.check(_lib.lib().ie_qlinear_allreduce(comm.handle, ctypes.byref(a), s),
+                   "qlinear_allreduce")
+    return out

@@ -1,0 +1,135 @@
+"""Tensor-parallel parity on one GPU: every rank's shard runs on the device,
+partials are summed with the reference's rank-order ``all_reduce``, and the
+result equals the reference's TP output (golden fixtures and the full-size
+CPU case).  Also: the fused row-parallel + all-reduce entry point at world 1,
+and the bounded peer wait ending in a timeout status (a loopback communicator
+whose peer never pushes), after which the context stays usable."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from ie_tpq import _lib
+from ie_tpq import formats as F
+from ie_tpq import weights as W
+from ie_tpq.comm import Communicator
+from ie_tpq.linear import qlinear
+from ie_tpq.sharding import ColumnParallelLinear, RowParallelLinear, Shard, all_reduce
+from ie_tpq.tensor_parallel import ShardedMLP, rms_norm
+from oracle import tpq_oracle as o
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 2e-2, 2e-3
+
+
+def test_list_all_reduce_is_the_reference_order_bitwise():
+    parts = [o.seeded_activations(7, 33, seed=s) for s in range(4)]
+    assert np.array_equal(all_reduce(parts), o.all_reduce(parts))
+
+
+def test_rms_norm_matches_the_reference():
+    x = o.seeded_activations(9, 896, seed=3)
+    w = np.linspace(0.5, 1.5, 896).astype(np.float32)
+    got = rms_norm(torch.from_numpy(x).cuda(), w).cpu().numpy()
+    np.testing.assert_allclose(got, o.rms_norm(x, w), rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_sharded_mlp_matches_the_golden_tp_output(golden, world):
+    x = golden["mlp_x"]
+    # the fixture's weights are the reference's int8-dequantized f32 weights;
+    # re-quantizing them with int8/axis 0 gives the same codes and scales
+    # within an ulp, so the dequantized weights agree to f32 rounding
+    qs = {name: W.quantize_integer(golden[f"mlp_{name}"], F.INT8)
+          for name in ("gate", "up", "down")}
+    for name in qs:
+        np.testing.assert_allclose(qs[name].dequantized(), golden[f"mlp_{name}"], rtol=1e-6)
+    xt = torch.from_numpy(x).cuda()
+    partials = [ShardedMLP(np.ones(64, np.float32), qs["gate"], qs["up"], qs["down"],
+                           Shard(r, world)).forward(xt) for r in range(world)]
+    got = (xt + all_reduce(partials)).cpu().numpy()
+    np.testing.assert_allclose(got, golden[f"mlp_out_{world}"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_full_size_cpu_case_tp2(golden_hashes, dtype):
+    """hidden 896, intermediate 4864, 64 tokens, TP=2, int8 per-channel (axis 0)."""
+    x, norm, gate, up, down = o.config1_inputs()
+    qs = {n: W.quantize_integer(w, F.INT8) for n, w in (("gate", gate), ("up", up),
+                                                        ("down", down))}
+    xt = torch.from_numpy(x).cuda().to(dtype)
+    parts = [ShardedMLP(norm, qs["gate"], qs["up"], qs["down"], Shard(r, 2)).forward(xt)
+             for r in range(2)]
+    got = (xt.float() + all_reduce([p.float() for p in parts])).cpu().numpy()
+    deq = {n: q.dequantized() for n, q in qs.items()}
+    want = o.tp_mlp(xt.float().cpu().numpy(), norm, deq["gate"], deq["up"], deq["down"], 2)
+    if dtype == torch.float32:
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+        assert float(np.sum(got.astype(np.float64))) == pytest.approx(
+            golden_hashes["config1_out_tp2_sum"], rel=1e-4, abs=1e-2)
+    else:
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL * 10)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_column_then_row_reproduces_the_unsharded_matmul(world):
+    """tests/test_tensor_parallel.py:59-72 with quantized weights on the device."""
+    x = o.seeded_activations(5, 256, seed=60)
+    first = W.quantize_grouped(o.seeded_weight(256, 512, seed=61))
+    second = W.quantize_grouped(o.seeded_weight(512, 256, seed=62))
+    whole = (x @ first.dequantized()) @ second.dequantized()
+    partials = []
+    for r in range(world):
+        sh = Shard(r, world)
+        hidden = ColumnParallelLinear(first, sh).forward(x)
+        partials.append(RowParallelLinear(second, sh).forward(hidden))
+    np.testing.assert_allclose(all_reduce(partials), whole, rtol=2e-3, atol=2e-3)
+
+
+def test_fused_allreduce_at_world_one_equals_the_plain_layer():
+    comm = Communicator(0, 1)
+    try:
+        q = W.quantize_integer(o.seeded_weight(512, 256, seed=70), F.INT8)
+        p = q.packed()
+        x = torch.from_numpy(o.seeded_activations(6, 512, seed=71)).cuda()
+        res = torch.from_numpy(o.seeded_activations(6, 256, seed=72)).cuda()
+        plain = qlinear(x, p, residual=res)
+        for _ in range(3):   # epochs advance; landing parity alternates
+            fused = qlinear(x, p, residual=res, comm=comm)
+            assert torch.equal(plain, fused)
+        y = comm.all_reduce(res)
+        assert torch.equal(y, res)
+        comm.check()
+    finally:
+        comm.close()
+
+
+def test_peer_that_never_arrives_ends_in_a_timeout_status():
+    comm = Communicator.loopback(world_size=2, timeout_s=0.05)
+    try:
+        q = W.quantize_integer(o.seeded_weight(256, 64, seed=80), F.INT8)
+        p = q.packed()
+        x = torch.from_numpy(o.seeded_activations(2, 256, seed=81)).cuda()
+        qlinear(x, p, comm=comm)
+        with pytest.raises(_lib.TimeoutError_):
+            comm.check()
+        comm.check()   # the status word was cleared
+        # the context is still healthy: a normal layer runs and is correct
+        y = qlinear(x, p).cpu().numpy()
+        np.testing.assert_allclose(y, x.cpu().numpy() @ q.dequantized(), rtol=1e-4, atol=1e-5)
+        comm.all_reduce(torch.ones(10, device="cuda"))
+        with pytest.raises(_lib.TimeoutError_):
+            comm.check()
+    finally:
+        comm.close()
+
+
+def test_communicator_rejects_oversized_requests():
+    comm = Communicator(0, 1, max_bytes=1024)
+    try:
+        with pytest.raises(ValueError):
+            comm.all_reduce(torch.ones(100000, device="cuda"))
+    finally:
+        comm.close()
