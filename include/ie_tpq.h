@@ -49,7 +49,7 @@ extern "C" {
 #define IE_AXIS_K 0          /* f32 scale[K]        (reference axis=0, its default) */
 #define IE_AXIS_N 1          /* f32 scale[N]        (reference axis=1)              */
 #define IE_AXIS_TENSOR 2     /* f32 scale[1]        (reference axis=None)           */
-#define IE_AXIS_GROUP128 3   /* f16 scale[N][K/128] and f16 zero[N][K/128]          */
+#define IE_AXIS_GROUP128 3   /* f16 scale[K/128][N] and f16 zero[K/128][N]          */
 
 /* element types */
 #define IE_DT_BF16 0
@@ -73,7 +73,7 @@ typedef struct ie_qweight {
                            holds k0..k0+7 with nibble p = code of k0 + {0,2,4,6,1,3,5,7}[p] */
   const void* scale;    /* per axis above; for gate/up pairs with IE_AXIS_K: f32 [2][k]
                            (gate table then up table) */
-  const void* zero;     /* f16 [n][k/128] for IE_AXIS_GROUP128, else NULL */
+  const void* zero;     /* f16 [k/128][n] for IE_AXIS_GROUP128, else NULL */
   int32_t int4_symmetric; /* INT4 only: 1 = codes stored as q+8 with an implicit zero of 8 */
   int32_t gate_up;        /* 1 = rows interleaved gate/up (use with IE_EPI_SILU_MUL) */
 } ie_qweight;
@@ -92,7 +92,8 @@ typedef struct ie_qlinear_args {
   const void* residual; /* [m][n] of out_dtype, row stride ldr, or NULL */
   int64_t ldr;
   int32_t epilogue;     /* IE_EPI_* flags */
-  int32_t algo;         /* 0 = auto; 1 = weight-streaming GEMV; 2 = tcgen05 tensor-core GEMM */
+  int32_t algo;         /* 0 = auto; 1 = weight-streaming GEMV; 2 = tcgen05 tensor-core GEMM
+                           (bf16/f16 activations, K % 128 == 0, 16-byte aligned rows) */
   void* workspace;      /* caller-owned scratch (see ie_qlinear_workspace_size), may be NULL */
   size_t workspace_bytes;
 } ie_qlinear_args;
@@ -127,8 +128,8 @@ int ie_round_to_float_format(const float* x, float* out, int64_t count, int32_t 
  * codes_kn: the reference's codes, [k][n] (int32 for INT8/INT4, f32 for FP8).
  * For IE_AXIS_GROUP128 pass codes_nk [n][k] int32 (the group view of
  * ie/quant/weights.py:51-70 on W.T), scale_f32/zero_f32 [n][k/128].
- * Outputs: packed codes in out_codes, f16 tables for GROUP128 in out_scale16 /
- * out_zero16.  *unrepresentable (device int32, may be NULL) counts FP8 codes
+ * Outputs: packed codes in out_codes, f16 tables [k/128][n] for GROUP128 in
+ * out_scale16 / out_zero16 (zero points must be exact in f16, else counted).  *unrepresentable (device int32, may be NULL) counts FP8 codes
  * that e4m3 cannot hold and were rounded to the nearest e4m3 value. */
 int ie_pack_weight(int32_t format, int32_t axis, int32_t int4_symmetric, int64_t k, int64_t n,
                    const void* codes, const float* scale_f32, const float* zero_f32,
@@ -144,8 +145,14 @@ int ie_dequantize(const ie_qweight* w, int32_t layout, int32_t out_dtype, void* 
  * (ie/parallel/sharding.py:51-66) and the projections of TorchBlock.forward
  * (ie/model/torch_transformer.py:36-38,60) and torch_backend.swiglu
  * (ie/kernels/torch_backend.py:125-127) on a packed shard. */
+/* Bytes of caller-owned workspace the call would use (split-K partials and
+ * tile tickets of the tensor-core kernel); the first 256-byte-rounded region
+ * holds tickets that must be zero before first use and are left zero. */
 size_t ie_qlinear_workspace_size(const ie_qlinear_args* a);
 int ie_qlinear(const ie_qlinear_args* a, void* stream);
+/* Error bits recorded by kernels (1 = a bounded pipeline wait expired);
+ * synchronous read of device state, optionally cleared. */
+int ie_kernel_status(uint32_t* bits, int32_t clear);
 
 /* ---- RMSNorm ------------------------------------------------------------------
  * Replaces ie/layers/functional.py:6-8 (rms_norm) and

@@ -52,6 +52,16 @@ int validate_linear(const ie_qlinear_args& a) {
   return IE_OK;
 }
 
+// Smallest token count routed to the tensor-core kernel under algo 0 (auto):
+// below it the weight-streaming kernel's CUDA-core FMAs keep up with HBM.
+constexpr int64_t kTcMinTokens = 2;
+
+bool use_tc(const ie_qlinear_args& a) {
+  if (a.algo == 1) return false;
+  if (a.algo == 2) return true;
+  return a.m >= kTcMinTokens && tc_usable(a);
+}
+
 }  // namespace
 }  // namespace ie
 
@@ -67,16 +77,22 @@ extern "C" int ie_last_error(char* buf, size_t n) {
 }
 
 extern "C" size_t ie_qlinear_workspace_size(const ie_qlinear_args* a) {
-  (void)a;
-  return 0;
+  if (!a || validate_linear(*a) != IE_OK || a->m == 0 || !use_tc(*a)) return 0;
+  return tc_workspace_bytes(*a);
 }
 
 extern "C" int ie_qlinear(const ie_qlinear_args* a, void* stream) {
   IE_CHECK(a, "qlinear: null args");
   int rc = validate_linear(*a);
   if (rc || a->m == 0) return rc;
-  IE_CHECK(a->algo != 2, "qlinear: the tensor-core path is not built into this library");
+  if (use_tc(*a)) return launch_qlinear_tc(*a, nullptr, as_stream(stream));
   return launch_qlinear_gemv(*a, nullptr, 0, as_stream(stream));
+}
+
+extern "C" int ie_kernel_status(uint32_t* bits, int32_t clear) {
+  IE_CHECK(bits, "kernel_status: null output");
+  *bits = tc_read_status(clear != 0);
+  return IE_OK;
 }
 
 extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* stream) {
@@ -86,7 +102,12 @@ extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* 
   IE_CHECK(!(a->epilogue & IE_EPI_SILU_MUL),
            "qlinear_allreduce: SILU_MUL belongs to the column-parallel gate/up layer");
   IE_CHECK(!a->w.gate_up, "qlinear_allreduce: gate/up pairs are column-parallel");
-  IE_CHECK(a->algo != 2, "qlinear_allreduce: the tensor-core path is not built into this library");
+  if (use_tc(*a)) {
+    ReduceCtx ctx;
+    rc = comm_context(c, &ctx, tc_tiles(*a), a->m * a->w.n);
+    if (rc) return rc;
+    return launch_qlinear_tc(*a, &ctx, as_stream(stream));
+  }
   int resident = 0;
   rc = gemv_resident_ctas(*a, &resident);
   if (rc) return rc;

@@ -139,6 +139,12 @@ int launch_qlinear_gemv(const ie_qlinear_args& a, const ReduceCtx* rc, int max_c
                         cudaStream_t s);
 int64_t gemv_tiles(const ie_qlinear_args& a);
 int gemv_resident_ctas(const ie_qlinear_args& a, int* out);
+// tcgen05 tensor-core path (qgemm_sm100.cu)
+bool tc_usable(const ie_qlinear_args& a);
+size_t tc_workspace_bytes(const ie_qlinear_args& a);
+int64_t tc_tiles(const ie_qlinear_args& a);
+int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_t s);
+uint32_t tc_read_status(bool clear);
 // Fills rc for a collective call of comm c after checking its limits.
 int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_rank);
 

@@ -50,7 +50,7 @@ struct GemvParams {
   const uint8_t* codes;
   int64_t row_bytes;
   const float* scale;     // per-K ([K] or [2][K]), per-N [N], per-tensor [1] or [2]
-  const __half* gscale;   // group-128 [N][K/128]
+  const __half* gscale;   // group-128 [K/128][N]
   const __half* gzero;
   int axis;
   int gate_up;
@@ -234,7 +234,7 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
             dot_vec<V, MT>(wv[u][r], xr, xstride, part);
             if constexpr (V == V_INT4G) {
               const int64_t g = (k0 + (int64_t)c * VI::kElems) / 128;
-              const int64_t gi = (r0 + r) * (p.K / 128) + g;
+              const int64_t gi = g * p.N + (r0 + r);
               const float s = __half2float(p.gscale[gi]);
               const float off = 128.0f + __half2float(p.gzero[gi]);
 #pragma unroll

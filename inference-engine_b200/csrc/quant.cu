@@ -375,15 +375,20 @@ __global__ void pack_int4_nk_kernel(const int32_t* __restrict__ codes, int64_t k
   }
 }
 
-// f32 group tables -> f16.  A zero point that f16 cannot hold exactly, or a
-// scale that overflows / flushes in f16, is counted as unrepresentable.
+// f32 group tables [n][k/128] (the reference's view order) -> f16 tables
+// [k/128][n], N-contiguous so one K group of 128 consecutive rows is one
+// contiguous run.  A zero point that f16 cannot hold exactly, or a scale that
+// overflows / flushes in f16, is counted as unrepresentable.
 __global__ void pack_group_tables_kernel(const float* __restrict__ scale,
-                                         const float* __restrict__ zero, int64_t count,
-                                         __half* __restrict__ s16, __half* __restrict__ z16,
+                                         const float* __restrict__ zero, int64_t n,
+                                         int64_t groups, __half* __restrict__ s16,
+                                         __half* __restrict__ z16,
                                          int32_t* __restrict__ unrepresentable) {
+  const int64_t count = n * groups;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float s = scale[i], z = zero[i];
+    const int64_t g = i / n, nn = i % n;
+    const float s = scale[nn * groups + g], z = zero[nn * groups + g];
     const __half hs = __float2half_rn(s), hz = __float2half_rn(z);
     s16[i] = hs;
     z16[i] = hz;
@@ -418,7 +423,7 @@ __device__ __forceinline__ float dequant_value(const ie_qweight& w, int64_t row,
   float q = packed_code(w, row, kk);
   const float* sc = static_cast<const float*>(w.scale);
   if (w.axis == IE_AXIS_GROUP128) {
-    const int64_t gi = row * (w.k / 128) + kk / 128;
+    const int64_t gi = (kk / 128) * w.n + row;
     const float s = __half2float(static_cast<const __half*>(w.scale)[gi]);
     const float z = __half2float(static_cast<const __half*>(w.zero)[gi]);
     return __fmul_rn(__fsub_rn(q, z), s);
@@ -539,9 +544,9 @@ extern "C" int ie_pack_weight(int32_t format, int32_t axis, int32_t int4_symmetr
         static_cast<const int32_t*>(codes), k, n, static_cast<uint32_t*>(out_codes));
     int rc = launch_status("pack_int4_nk_kernel");
     if (rc) return rc;
-    const int64_t groups = n * (k / 128);
-    pack_group_tables_kernel<<<grid_for(groups), kThreads, 0, s>>>(
-        scale_f32, zero_f32, groups, static_cast<__half*>(out_scale16),
+    const int64_t groups = k / 128;
+    pack_group_tables_kernel<<<grid_for(groups * n), kThreads, 0, s>>>(
+        scale_f32, zero_f32, n, groups, static_cast<__half*>(out_scale16),
         static_cast<__half*>(out_zero16), unrepresentable);
     return launch_status("pack_group_tables_kernel");
   }

@@ -15,6 +15,22 @@ from .packed import PackedWeight
 
 ALGO_AUTO, ALGO_GEMV, ALGO_TCGEN05 = 0, 1, 2
 
+# One zero-initialised workspace per device, grown on demand.  The kernels
+# leave its ticket region zero, so consecutive calls on one stream share it;
+# calls on concurrent streams must pass their own ``workspace=``.
+_WORKSPACE: dict = {}
+
+
+def shared_workspace(nbytes: int, device):
+    torch = require_cuda()
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _WORKSPACE.get(key)
+    if ws is None or ws.numel() < nbytes:
+        size = max(nbytes, 2 * ws.numel() if ws is not None else 1 << 20)
+        ws = torch.zeros(size, dtype=torch.uint8, device=device)
+        _WORKSPACE[key] = ws
+    return ws
+
 
 def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=False,
                algo=ALGO_AUTO, workspace=None) -> _lib.QLinearArgs:
@@ -53,7 +69,8 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
 
 
 def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | None = None,
-            out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None):
+            out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None,
+            workspace=None):
     """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce.
 
     x: CUDA tensor ``[M, K]`` (bf16 / f16 / f32).  bias: f32 ``[N]``.  residual:
@@ -70,6 +87,13 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
     if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
         bias = bias.to(torch.float32).contiguous()
     a = build_args(x, w, out, bias=bias, residual=residual, silu_mul=silu_mul, algo=algo)
+    need = _lib.lib().ie_qlinear_workspace_size(ctypes.byref(a))
+    if need:
+        ws = workspace if workspace is not None else shared_workspace(need, x.device)
+        if ws.numel() * ws.element_size() < need:
+            raise ValueError(f"workspace of {ws.numel() * ws.element_size()} bytes < {need} needed")
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = ws.numel() * ws.element_size()
     s = _lib.stream_ptr(stream)
     if comm is None:
         _lib.check(_lib.lib().ie_qlinear(ctypes.byref(a), s), "qlinear")

@@ -9,8 +9,8 @@ On the device every output column becomes a K-contiguous row:
               nibble p holding k0 + (0,2,4,6,1,3,5,7)[p] so one mask+or yields
               the (k0+2p, k0+2p+1) pair; symmetric codes are stored +8;
   * scales -- f32 ``[K]`` (reference axis 0), ``[N]`` (axis 1) or ``[1]``;
-              group-128: f16 scale and zero ``[N][K/128]`` (a documented cast of
-              the reference's bit-exact f32 tables).
+              group-128: f16 scale and zero ``[K/128][N]`` (a documented cast of
+              the reference's bit-exact f32 tables, N-contiguous per K group).
 
 Gate/up pairs for the fused SiLU*up epilogue interleave rows (row 2j = gate
 column j, row 2j+1 = up column j); per-K and per-tensor tables then hold the
@@ -126,8 +126,8 @@ class PackedWeight:
         if axis == _lib.IE_AXIS_GROUP128:
             zero32 = torch.from_numpy(np.ascontiguousarray(qw.zero_point, dtype=np.float32)
                                       .reshape(-1)).to(dev)
-            scale = torch.empty((n, k // 128), dtype=torch.float16, device=dev)
-            zero = torch.empty((n, k // 128), dtype=torch.float16, device=dev)
+            scale = torch.empty((k // 128, n), dtype=torch.float16, device=dev)
+            zero = torch.empty((k // 128, n), dtype=torch.float16, device=dev)
             _lib.check(_lib.lib().ie_pack_weight(
                 fmt, axis, 0, k, n, codes_src.data_ptr(), scale32.data_ptr(), zero32.data_ptr(),
                 codes.data_ptr(), scale.data_ptr(), zero.data_ptr(), counter.data_ptr(), stream),
@@ -169,10 +169,12 @@ class PackedWeight:
         """Output columns [n0, n1) of the reference weight (a column shard)."""
         if self.gate_up:
             raise ValueError("shard gate and up before pairing them")
-        scale = self.scale
-        if self.axis in (_lib.IE_AXIS_N, _lib.IE_AXIS_GROUP128):
+        scale, zero = self.scale, self.zero
+        if self.axis == _lib.IE_AXIS_N:
             scale = self.scale[n0:n1]
-        zero = self.zero[n0:n1] if self.zero is not None else None
+        elif self.axis == _lib.IE_AXIS_GROUP128:
+            scale = self.scale[:, n0:n1].contiguous()
+            zero = self.zero[:, n0:n1].contiguous()
         return PackedWeight(fmt=self.fmt, axis=self.axis, k=self.k, n=n1 - n0,
                             codes=self.codes[n0:n1], scale=scale, zero=zero,
                             int4_symmetric=self.int4_symmetric)
@@ -191,8 +193,8 @@ class PackedWeight:
         if self.axis == _lib.IE_AXIS_K:
             scale = self.scale[k0:k1].contiguous()
         elif self.axis == _lib.IE_AXIS_GROUP128:
-            scale = self.scale[:, k0 // 128:k1 // 128].contiguous()
-            zero = self.zero[:, k0 // 128:k1 // 128].contiguous()
+            scale = self.scale[k0 // 128:k1 // 128].contiguous()
+            zero = self.zero[k0 // 128:k1 // 128].contiguous()
         return PackedWeight(fmt=self.fmt, axis=self.axis, k=k1 - k0, n=self.n, codes=codes,
                             scale=scale, zero=zero, int4_symmetric=self.int4_symmetric)
 
@@ -204,15 +206,15 @@ class PackedWeight:
                 (up.fmt, up.axis, up.k, up.n, up.int4_symmetric):
             raise ValueError("gate and up must share format, scale axis and shape")
         codes = torch.stack([gate.codes, up.codes], dim=1).reshape(2 * gate.n, -1).contiguous()
+        zero = None
         if gate.axis in (_lib.IE_AXIS_K, _lib.IE_AXIS_TENSOR):
             scale = torch.cat([gate.scale.reshape(-1), up.scale.reshape(-1)]).contiguous()
-        else:
-            scale = torch.stack([gate.scale, up.scale], dim=1).reshape(
-                (2 * gate.n,) + tuple(gate.scale.shape[1:])).contiguous()
-        zero = None
-        if gate.zero is not None:
-            zero = torch.stack([gate.zero, up.zero], dim=1).reshape(
-                (2 * gate.n,) + tuple(gate.zero.shape[1:])).contiguous()
+        elif gate.axis == _lib.IE_AXIS_N:
+            scale = torch.stack([gate.scale, up.scale], dim=1).reshape(2 * gate.n).contiguous()
+        else:   # group tables [G][N]: interleave along N
+            g = gate.scale.shape[0]
+            scale = torch.stack([gate.scale, up.scale], dim=2).reshape(g, 2 * gate.n).contiguous()
+            zero = torch.stack([gate.zero, up.zero], dim=2).reshape(g, 2 * gate.n).contiguous()
         return PackedWeight(fmt=gate.fmt, axis=gate.axis, k=gate.k, n=2 * gate.n, codes=codes,
                             scale=scale, zero=zero, int4_symmetric=gate.int4_symmetric,
                             gate_up=True)
@@ -230,10 +232,11 @@ def concat_rows(parts: list["PackedWeight"]) -> "PackedWeight":
             raise ValueError("concatenated weights must share format, scale axis and K")
     if first.axis not in (_lib.IE_AXIS_N, _lib.IE_AXIS_GROUP128):
         raise ValueError("only per-N or group-128 tables can be concatenated along N")
-    zero = torch.cat([p.zero for p in parts]) if first.zero is not None else None
+    dim = 1 if first.axis == _lib.IE_AXIS_GROUP128 else 0
+    zero = torch.cat([p.zero for p in parts], dim=1).contiguous() if first.zero is not None else None
     return PackedWeight(fmt=first.fmt, axis=first.axis, k=first.k, n=sum(p.n for p in parts),
                         codes=torch.cat([p.codes for p in parts]).contiguous(),
-                        scale=torch.cat([p.scale for p in parts]).contiguous(), zero=zero,
+                        scale=torch.cat([p.scale for p in parts], dim=dim).contiguous(), zero=zero,
                         int4_symmetric=first.int4_symmetric)
 
 
@@ -264,7 +267,7 @@ def quantize_on_device(w, scheme: str, axis: int | None = 0) -> "PackedWeight":
                    "quantize_integer")
         del view
         packed = torch.empty((n, k // 2), dtype=torch.uint8, device=dev)
-        s16 = torch.empty((n, k // 128), dtype=torch.float16, device=dev)
+        s16 = torch.empty((k // 128, n), dtype=torch.float16, device=dev)
         z16 = torch.empty_like(s16)
         bad = torch.zeros(1, dtype=torch.int32, device=dev)
         _lib.check(L.ie_pack_weight(_lib.IE_FMT_INT4, _lib.IE_AXIS_GROUP128, 0, k, n,
