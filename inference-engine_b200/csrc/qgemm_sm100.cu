@@ -3,18 +3,23 @@
 //
 // The weight is the MMA's A operand (M = 128 output rows per tile) and the
 // token batch is its N dimension (16..256), so decode batches of 16 and
-// prefill batches use the same kernel.  Per CTA (192 threads, one per SM):
+// prefill batches use the same kernel.  Per CTA (320 threads, one per SM):
 //
-//   warp 0      TMA producer: packed weight tile [128 rows x 128 K] and the
+//   warp 0      TMA producer: packed weight tile [128 rows x 128 K], the
 //               activation tile [BN tokens x 128 K] (bf16/f16, 128-byte
-//               swizzle) into a ring of shared-memory stages (no multicast).
+//               swizzle) and the stage's scale tables (group-128 scale/zero
+//               rows, or the per-K scales) into a ring of shared-memory stages
+//               (no multicast).
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma
-//               (kind::f16, f32 accumulator in TMEM, 8 x K=16 per stage) and
-//               tcgen05.commit releases the stage.
-//   warps 2..5  dequantize each weight stage in registers (int4 pairs widened
-//               with one mask+or into the mantissas of a bf16x2 / f16x2, zero
+//               (kind::f16 with f16 operands, f32 accumulator in TMEM,
+//               8 x K=16 per stage) and tcgen05.commit releases the stage.
+//   warps 2..9  dequantize each weight stage in registers (int4 pairs widened
+//               with one mask+or into the mantissas of an f16x2, zero
 //               subtracted exactly, group scale applied once) into the
-//               canonical SW128 K-major layout of the A ring; then, per work
+//               canonical SW128 K-major layout of the A ring; bf16 activation
+//               tiles are converted to f16 in place (f16 keeps 11 significant
+//               bits, so the dequantized weight carries at most 2^-12 relative
+//               rounding, against 2^-9 for bf16); then, per work
 //               unit, read the accumulator with tcgen05.ld and run the
 //               epilogue (split-K reduction in split order, per-N / per-tensor
 //               scale, bias, SiLU*up, residual, store or all-reduce push).
@@ -36,11 +41,13 @@
 namespace ie {
 namespace tc {
 
-constexpr int kThreads = 192;
+constexpr int kDqWarps = 8;     // dequant + epilogue warps (two per SM sub-partition)
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kThreads = 64 + kDqThreads;
 constexpr int kTileN = 128;     // weight rows per tile = MMA M
 constexpr int kBK = 128;        // K per stage (one int4 group)
-constexpr int kAStages = 2;     // dequantized A ring depth
-constexpr int kABytes = kTileN * kBK * 2;   // one A stage (bf16/f16)
+constexpr int kMaxAStages = 4;  // dequantized A ring depth (4 for decode tiles, 2 for wide)
+constexpr int kABytes = kTileN * kBK * 2;   // one A stage (f16)
 constexpr uint64_t kWaitNs = 2000000000ull; // bounded mbarrier waits
 
 enum Fmt { F_INT4G = 0, F_INT4SYM = 1, F_INT8 = 2, F_FP8 = 3 };
@@ -52,6 +59,7 @@ constexpr uint32_t kErrWait = 1u;
 struct TcParams {
   int64_t M, K, N;          // tokens, contraction, packed rows
   int axis, gate_up, epilogue, out_dtype;
+  int x_bf16;               // activations arrive as bf16 and are converted to f16
   const float* scale;       // per-K [K] / [2][K], per-N [N], per-tensor [1] / [2]
   const __half* gscale;     // group-128 [K/128][N]
   const __half* gzero;
@@ -63,7 +71,11 @@ struct TcParams {
   int bn;                   // tokens per tile (MMA N)
   int n_tiles, m_tiles, splits, kstages;   // kstages = K / kBK
   int ns;                   // TMA ring depth
+  int na;                   // A ring depth
   int w_stage_bytes;        // packed weight bytes per stage
+  int t_kind;               // stage tables: 0 none, 1 group s/z f16 [128] each, 2 per-K f32
+  int t_rows;               // per-K tables: 1, or 2 for gate/up pairs
+  int t_stage_bytes;        // table bytes per stage (1024-aligned slot)
   float* ws;                // split-K partials [splits][M][N]
   uint32_t* counters;       // per (m_tile, n_tile) tickets, self-resetting
 };
@@ -158,6 +170,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), version 1 for sm_100.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -227,11 +251,11 @@ __device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
 
 // Dequantize one work item (row r of the tile, 16-byte input chunk c) of the
 // stage at K offset k0 into the A stage buffer `a` (two 64-wide SW128 blocks).
-template <int FMT, typename TA>
+template <int FMT>
 __device__ __forceinline__ void dequant_item(const TcParams& p, const uint8_t* wst, uint8_t* a,
-                                             int r, int c, int64_t n_row, int64_t k0,
+                                             int r, int c, int64_t n_row, const float* tbl,
                                              uint32_t g_off, uint32_t g_scale) {
-  using AT = AType<TA>;
+  using AT = AType<__half>;
   const int row_bytes = p.w_stage_bytes / kTileN;
   const uint4 in = *reinterpret_cast<const uint4*>(wst + r * row_bytes + c * 16);
   const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
@@ -254,8 +278,7 @@ __device__ __forceinline__ void dequant_item(const TcParams& p, const uint8_t* w
     constexpr int kPer = (FMT == F_INT4SYM) ? 32 : 16;
     const int kbase = c * kPer;
     const float* sk = nullptr;
-    if (p.axis == IE_AXIS_K)
-      sk = p.scale + (p.gate_up ? (n_row & 1) * p.K : 0) + k0 + kbase;
+    if (p.axis == IE_AXIS_K) sk = tbl + (p.t_rows == 2 ? (n_row & 1) * kBK : 0) + kbase;
 #pragma unroll
     for (int j = 0; j < kPer / 8; ++j) {
       float v[8];
@@ -273,7 +296,7 @@ __device__ __forceinline__ void dequant_item(const TcParams& p, const uint8_t* w
         } else {
           q = e4m3_to_f32(w4[idx >> 2] >> (8 * (idx & 3)));
         }
-        v[e] = sk ? q * __ldg(sk + idx) : q;
+        v[e] = sk ? q * sk[idx] : q;
       }
       const int kk = kbase + 8 * j;
       uint8_t* dst = a + (kk >> 6) * (kTileN * 128) + sw128_offset(r, (kk & 63) >> 3);
@@ -297,24 +320,39 @@ __device__ __forceinline__ float load_val(const void* in, int dt, int64_t i) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int FMT, typename TA>
+// bf16 -> f16 of one 16-byte chunk (8 values), in place.
+__device__ __forceinline__ void bf16_to_f16_chunk(uint4* p) {
+  uint4 v = *p;
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(w[i] << 16);
+    const float hi = __uint_as_float(w[i] & 0xFFFF0000u);
+    w[i] = AType<__half>::pack(lo, hi);
+  }
+  *p = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                 TcParams p, ReduceCtx rc, int reduce) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int ns = p.ns;
+  const int ns = p.ns, na = p.na;
   const int x_stage_bytes = p.bn * kBK * 2;
-  uint8_t* a_ring = smem;                                   // kAStages x 32 KB
-  uint8_t* x_ring = a_ring + kAStages * kABytes;            // ns x x_stage_bytes
+  uint8_t* a_ring = smem;                                   // na x 32 KB
+  uint8_t* x_ring = a_ring + na * kABytes;                  // ns x x_stage_bytes
   uint8_t* w_ring = x_ring + ns * x_stage_bytes;            // ns x w_stage_bytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(w_ring + ns * p.w_stage_bytes);
+  uint8_t* t_ring = w_ring + ns * p.w_stage_bytes;          // ns x t_stage_bytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + ns * p.t_stage_bytes);
   uint64_t* full = bars;                 // [ns]  TMA landed (count 1 + tx)
   uint64_t* empty = full + ns;           // [ns]  MMA done + dequant done (count 2)
-  uint64_t* afull = empty + ns;          // [kAStages] dequant -> MMA (count 1)
-  uint64_t* aempty = afull + kAStages;   // [kAStages] MMA -> dequant (count 1)
-  uint64_t* accfull = aempty + kAStages; // MMA -> epilogue
+  uint64_t* afull = empty + ns;          // [na] dequant -> MMA (count 1)
+  uint64_t* aempty = afull + na;         // [na] MMA -> dequant (count 1)
+  uint64_t* accfull = aempty + na;       // MMA -> epilogue
   uint64_t* accempty = accfull + 1;      // epilogue -> MMA (count 1)
   uint64_t* mma_done = accempty + 1;     // final commit: all MMAs retired
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -330,7 +368,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);
     }
-    for (int s = 0; s < kAStages; ++s) {
+    for (int s = 0; s < na; ++s) {
       mbar_init(&afull[s], 1);
       mbar_init(&aempty[s], 1);
     }
@@ -376,9 +414,18 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             *abort_flag = 1;
             break;
           }
-          mbar_expect_tx(&full[s], (uint32_t)(p.w_stage_bytes + x_stage_bytes));
+          const uint32_t tbytes = p.t_kind == 1 ? 2 * kTileN * 2
+                                  : (p.t_kind == 2 ? (uint32_t)(p.t_rows * kBK * 4) : 0u);
+          mbar_expect_tx(&full[s], (uint32_t)(p.w_stage_bytes + x_stage_bytes) + tbytes);
           tma_load_2d(w_ring + s * p.w_stage_bytes, &tm_w, ks * (p.w_stage_bytes / kTileN),
                       nt * kTileN, &full[s]);
+          uint8_t* ts = t_ring + s * p.t_stage_bytes;
+          if (p.t_kind == 1) {
+            tma_load_2d(ts, &tm_s, nt * kTileN, ks, &full[s]);
+            tma_load_2d(ts + kTileN * 2, &tm_z, nt * kTileN, ks, &full[s]);
+          } else if (p.t_kind == 2) {
+            tma_load_2d(ts, &tm_s, ks * kBK, 0, &full[s]);
+          }
           uint8_t* xs = x_ring + s * x_stage_bytes;
           tma_load_2d(xs, &tm_x, ks * kBK, mt * p.bn, &full[s]);
           tma_load_2d(xs + p.bn * 128, &tm_x, ks * kBK + 64, mt * p.bn, &full[s]);
@@ -396,7 +443,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(std::is_same<TA, __nv_bfloat16>::value ? 1 : 0, p.bn);
+      const uint32_t idesc = make_idesc(0, p.bn);   // f16 x f16 -> f32
       int it = 0, ait = 0, unit_i = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
@@ -408,9 +455,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
         tc_fence_after();
         for (int ks = ks0; ks < ks1; ++ks, ++it, ++ait) {
-          const int s = it % ns, a = ait % kAStages;
+          const int s = it % ns, a = ait % na;
           if (!mbar_wait(&full[s], (it / ns) & 1, abort_flag) ||
-              !mbar_wait(&afull[a], (ait / kAStages) & 1, abort_flag)) {
+              !mbar_wait(&afull[a], (ait / na) & 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -439,44 +486,51 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       }
     }
   } else {
-    // ---------------------- dequantize + epilogue (128 threads) ----------------------
+    // ---------------------- dequantize + epilogue (256 threads) ----------------------
     const int dt = threadIdx.x - 64;
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter ..
+    const int half = (warp - 2) >> 2;             // which half of the columns
     const int row = quarter * 32 + lane;          // accumulator row of this thread
     constexpr int kChunks = (FMT == F_INT4G || FMT == F_INT4SYM) ? 4 : 8;  // per row per stage
+    constexpr int kItems = kTileN * kChunks / kDqThreads;                  // per thread
     int it = 0, ait = 0, unit_i = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
       for (int ks = ks0; ks < ks1; ++ks, ++it, ++ait) {
-        const int s = it % ns, a = ait % kAStages;
+        const int s = it % ns, a = ait % na;
         if (!mbar_wait(&full[s], (it / ns) & 1, abort_flag) ||
-            !mbar_wait(&aempty[a], ((ait / kAStages) & 1) ^ 1, abort_flag)) {
+            !mbar_wait(&aempty[a], ((ait / na) & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
         const uint8_t* wst = w_ring + s * p.w_stage_bytes;
         uint8_t* ast = a_ring + a * kABytes;
-        const int64_t k0 = (int64_t)ks * kBK;
-        for (int item = dt; item < kTileN * kChunks; item += 128) {
+        const uint8_t* tst = t_ring + s * p.t_stage_bytes;
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+          const int item = dt + i * kDqThreads;
           const int r = item / kChunks, c = item % kChunks;
           const int64_t n_row = (int64_t)nt * kTileN + r;
           uint32_t g_off = 0, g_scale = 0;
           if constexpr (FMT == F_INT4G) {
-            float s_ = 0.0f, z_ = 0.0f;
-            if (n_row < p.N) {
-              const int64_t gi = (k0 / 128) * p.N + n_row;
-              s_ = __half2float(p.gscale[gi]);
-              z_ = __half2float(p.gzero[gi]);
-            }
-            g_off = AType<TA>::splat(AType<TA>::kBias + z_);
-            g_scale = AType<TA>::splat(s_);
+            // rows past N were zero-filled by the TMA, so s = 0 there
+            const __half s_ = reinterpret_cast<const __half*>(tst)[r];
+            const __half z_ = reinterpret_cast<const __half*>(tst + kTileN * 2)[r];
+            const __half zb = __hadd(z_, __float2half_rn(AType<__half>::kBias));
+            g_off = (uint32_t)__half_as_ushort(zb) * 0x10001u;
+            g_scale = (uint32_t)__half_as_ushort(s_) * 0x10001u;
           }
-          dequant_item<FMT, TA>(p, wst, ast, r, c, n_row, k0, g_off, g_scale);
+          dequant_item<FMT>(p, wst, ast, r, c, n_row, reinterpret_cast<const float*>(tst),
+                            g_off, g_scale);
+        }
+        if (p.x_bf16) {
+          uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes);
+          for (int i = dt; i < x_stage_bytes / 16; i += kDqThreads) bf16_to_f16_chunk(xs + i);
         }
         fence_proxy_async();
-        named_sync(1, 128);
+        named_sync(1, kDqThreads);
         if (dt == 0) {
           mbar_arrive(&afull[a]);
           mbar_arrive(&empty[s]);
@@ -498,19 +552,21 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         if (p.axis == IE_AXIS_N) nscale = p.scale[n];
         else if (p.axis == IE_AXIS_TENSOR) nscale = p.scale[p.gate_up ? (n & 1) : 0];
       }
-      // pass 1: TMEM -> registers -> (workspace | final)
-      for (int c0 = 0; c0 < p.bn; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+      // pass 1: TMEM -> registers -> (workspace | final); this warp owns the
+      // columns [c_lo, c_hi) of its lane quarter
+      const int c_lo = half * (p.bn / 2), c_hi = c_lo + p.bn / 2;
+      for (int c0 = c_lo; c0 < c_hi; c0 += 8) {
+        float v[8];
+        tmem_ld8(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
         if (split) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < 8; ++j) {
             const int64_t m = m0 + c0 + j;
             if (m < p.M && n < p.N) p.ws[((int64_t)sp * p.M + m) * p.N + n] = v[j];
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < 8; ++j) {
             // finalize token m0+c0+j for row n
             const int64_t m = m0 + c0 + j;
             float val = v[j] * nscale;
@@ -538,7 +594,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
       tc_fence_before();
-      named_sync(1, 128);
+      named_sync(1, kDqThreads);
       if (dt == 0) mbar_arrive(accempty);
 
       const int tile_id = mt * p.n_tiles + nt;
@@ -546,21 +602,22 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (split) {
         // ticket: the last split to arrive sums all splits in split order
         __threadfence();
-        named_sync(1, 128);
+        named_sync(1, kDqThreads);
         if (dt == 0) {
           const uint32_t t = atomicAdd(&p.counters[tile_id], 1u);
           *s_ticket = (t == (uint32_t)(p.splits - 1)) ? 1 : 0;
         }
-        named_sync(1, 128);
+        named_sync(1, kDqThreads);
         finalize_here = *s_ticket != 0;
         if (finalize_here) {
           __threadfence();
-          for (int j = 0; j < p.bn; ++j) {
+          for (int j = c_lo; j < c_hi; ++j) {
             const int64_t m = m0 + j;
             float acc = 0.0f;
             if (m < p.M && n < p.N) {
-              acc = p.ws[m * p.N + n];
-              for (int q = 1; q < p.splits; ++q) acc += p.ws[((int64_t)q * p.M + m) * p.N + n];
+              acc = __ldcg(p.ws + m * p.N + n);
+              for (int q = 1; q < p.splits; ++q)
+                acc += __ldcg(p.ws + ((int64_t)q * p.M + m) * p.N + n);
             }
             float val = acc * nscale;
             if (p.epilogue & IE_EPI_SILU_MUL) {
@@ -588,7 +645,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
       if (reduce && finalize_here) {
-        named_sync(1, 128);
+        named_sync(1, kDqThreads);
         if (dt < rc.world) {
           __threadfence_system();
           st_release_sys(rc.flags[dt] + (int64_t)tile_id * kMaxWorld + rc.rank, epoch);
@@ -664,8 +721,9 @@ EncodeFn encode_fn() {
 }
 
 struct Plan {
-  int fmt = 0, bn = 16, m_tiles = 1, n_tiles = 1, splits = 1, kstages = 1, ns = 2;
+  int fmt = 0, bn = 16, m_tiles = 1, n_tiles = 1, splits = 1, kstages = 1, ns = 2, na = 2;
   int w_stage_bytes = 0;
+  int t_kind = 0, t_rows = 0, t_stage_bytes = 0;
   size_t smem = 0;
   size_t ws_bytes = 0;       // counters + partials
   size_t counters_bytes = 0;
@@ -707,6 +765,9 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   const int tiles = pl.n_tiles * pl.m_tiles;
   for (int s = 1; s <= (allow_split ? 16 : 1); ++s) {
     if (s > 1 && pl.kstages < 2 * s) break;
+    // every split must own at least one stage: (s-1) * ceil(kstages/s) < kstages
+    const int per = (pl.kstages + s - 1) / s;
+    if ((s - 1) * per >= pl.kstages) continue;
     const int units = tiles * s;
     const int waves = (units + sms - 1) / sms;
     const double eff = (double)units / ((double)waves * sms);
@@ -717,12 +778,22 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
       pl.splits = s;
     }
   }
+  if (a.w.axis == IE_AXIS_GROUP128) {
+    pl.t_kind = 1;
+    pl.t_stage_bytes = 1024;
+  } else if (a.w.axis == IE_AXIS_K) {
+    pl.t_kind = 2;
+    pl.t_rows = a.w.gate_up ? 2 : 1;
+    pl.t_stage_bytes = 1024;
+  }
   const size_t x_stage = (size_t)pl.bn * kBK * 2;
   const size_t budget = 220 * 1024;
-  const size_t fixed = (size_t)kAStages * kABytes + 1024 + 256;
-  pl.ns = (int)std::min<size_t>(8, (budget - fixed) / (x_stage + pl.w_stage_bytes));
+  pl.na = pl.bn <= 64 ? kMaxAStages : 2;
+  const size_t fixed = (size_t)pl.na * kABytes + 1024 + 256;
+  const size_t per = x_stage + pl.w_stage_bytes + pl.t_stage_bytes;
+  pl.ns = (int)std::min<size_t>(8, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
-  pl.smem = fixed + (size_t)pl.ns * (x_stage + pl.w_stage_bytes) + 8 * (2 * pl.ns + 2 * kAStages + 3) + 16;
+  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 3) + 16;
   if (pl.splits > 1) {
     pl.counters_bytes = (((size_t)tiles * 4) + 255) / 256 * 256;
     pl.ws_bytes = pl.counters_bytes + (size_t)pl.splits * M * a.w.n * 4;
@@ -735,20 +806,22 @@ bool tc_eligible(const ie_qlinear_args& a) {
   if (a.w.k % kBK) return false;
   if (((uintptr_t)a.x & 15) || ((a.ldx * 2) & 15)) return false;
   if (((uintptr_t)a.w.codes & 15)) return false;
+  if (((uintptr_t)a.w.scale & 15)) return false;
+  if (a.w.axis == IE_AXIS_GROUP128 && ((a.w.n % 8) || ((uintptr_t)a.w.zero & 15))) return false;
   return encode_fn() != nullptr;
 }
 
-template <int FMT, typename TA>
+template <int FMT>
 int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw,
-                 const CUtensorMap& tx, const TcParams& prm, const ReduceCtx* rc,
-                 cudaStream_t s) {
-  auto kern = qgemm_tc_kernel<FMT, TA>;
+                 const CUtensorMap& tx, const CUtensorMap& ts, const CUtensorMap& tz,
+                 const TcParams& prm, const ReduceCtx* rc, cudaStream_t s) {
+  auto kern = qgemm_tc_kernel<FMT>;
   IE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)pl.smem));
   const int units = pl.n_tiles * pl.m_tiles * pl.splits;
   const int grid = std::min(units, sm_count());
   ReduceCtx none{};
-  kern<<<grid, kThreads, pl.smem, s>>>(tw, tx, prm, rc ? *rc : none, rc ? 1 : 0);
+  kern<<<grid, kThreads, pl.smem, s>>>(tw, tx, ts, tz, prm, rc ? *rc : none, rc ? 1 : 0);
   return launch_status("qgemm_tc_kernel");
 }
 
@@ -797,6 +870,29 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(x): %d", (int)r);
   }
+  CUtensorMap ts = tw, tz = tw;   // unused copies when the stage carries no tables
+  if (pl.t_kind == 1) {
+    const cuuint64_t dims[2] = {(cuuint64_t)a.w.n, (cuuint64_t)(a.w.k / 128)};
+    const cuuint64_t strides[1] = {(cuuint64_t)a.w.n * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTileN, 1};
+    const cuuint32_t estr[2] = {1, 1};
+    for (int i = 0; i < 2; ++i) {
+      CUresult r = enc(i ? &tz : &ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                       const_cast<void*>(i ? a.w.zero : a.w.scale), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(groups): %d", (int)r);
+    }
+  } else if (pl.t_kind == 2) {
+    const cuuint64_t dims[2] = {(cuuint64_t)a.w.k, (cuuint64_t)pl.t_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)a.w.k * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)pl.t_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(a.w.scale), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(k scales): %d", (int)r);
+  }
   TcParams prm{};
   prm.M = a.m;
   prm.K = a.w.k;
@@ -822,25 +918,21 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   prm.splits = pl.splits;
   prm.kstages = pl.kstages;
   prm.ns = pl.ns;
+  prm.na = pl.na;
   prm.w_stage_bytes = pl.w_stage_bytes;
+  prm.t_kind = pl.t_kind;
+  prm.t_rows = pl.t_rows;
+  prm.t_stage_bytes = pl.t_stage_bytes;
   if (pl.splits > 1) {
     prm.counters = static_cast<uint32_t*>(a.workspace);
     prm.ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pl.counters_bytes);
   }
-  const bool bf = a.act_dtype == IE_DT_BF16;
+  prm.x_bf16 = a.act_dtype == IE_DT_BF16 ? 1 : 0;
   switch (pl.fmt) {
-    case F_INT4G:
-      return bf ? launch_typed<F_INT4G, __nv_bfloat16>(a, pl, tw, tx, prm, rc, s)
-                : launch_typed<F_INT4G, __half>(a, pl, tw, tx, prm, rc, s);
-    case F_INT4SYM:
-      return bf ? launch_typed<F_INT4SYM, __nv_bfloat16>(a, pl, tw, tx, prm, rc, s)
-                : launch_typed<F_INT4SYM, __half>(a, pl, tw, tx, prm, rc, s);
-    case F_INT8:
-      return bf ? launch_typed<F_INT8, __nv_bfloat16>(a, pl, tw, tx, prm, rc, s)
-                : launch_typed<F_INT8, __half>(a, pl, tw, tx, prm, rc, s);
-    default:
-      return bf ? launch_typed<F_FP8, __nv_bfloat16>(a, pl, tw, tx, prm, rc, s)
-                : launch_typed<F_FP8, __half>(a, pl, tw, tx, prm, rc, s);
+    case F_INT4G: return launch_typed<F_INT4G>(a, pl, tw, tx, ts, tz, prm, rc, s);
+    case F_INT4SYM: return launch_typed<F_INT4SYM>(a, pl, tw, tx, ts, tz, prm, rc, s);
+    case F_INT8: return launch_typed<F_INT8>(a, pl, tw, tx, ts, tz, prm, rc, s);
+    default: return launch_typed<F_FP8>(a, pl, tw, tx, ts, tz, prm, rc, s);
   }
 }
 
