@@ -2,34 +2,40 @@
 // one-shot all-reduce fused into the epilogue.
 //
 // The weight is the MMA's A operand (M = 128 output rows per tile) and the
-// token batch is its N dimension (16..256), so decode batches of 16 and
-// prefill batches use the same kernel.  Per CTA (320 threads, one per SM):
+// token batch is its N dimension (16..256), so decode batches and prefill
+// batches use the same kernel.  Per CTA (320 threads, one CTA per SM):
 //
-//   warp 0      TMA producer: packed weight tile [128 rows x 128 K], the
-//               activation tile [BN tokens x 128 K] (bf16/f16, 128-byte
-//               swizzle) and the stage's scale tables (group-128 scale/zero
-//               rows, or the per-K scales) into a ring of shared-memory stages
-//               (no multicast).
-//   warp 1      MMA issuer: one elected thread issues tcgen05.mma
-//               (kind::f16 with f16 operands, f32 accumulator in TMEM,
-//               8 x K=16 per stage) and tcgen05.commit releases the stage.
-//   warps 2..9  dequantize each weight stage in registers (int4 pairs widened
-//               with one mask+or into the mantissas of an f16x2, zero
-//               subtracted exactly, group scale applied once) into the
-//               canonical SW128 K-major layout of the A ring; bf16 activation
-//               tiles are converted to f16 in place (f16 keeps 11 significant
-//               bits, so the dequantized weight carries at most 2^-12 relative
-//               rounding, against 2^-9 for bf16); then, per work
-//               unit, read the accumulator with tcgen05.ld and run the
-//               epilogue (split-K reduction in split order, per-N / per-tensor
-//               scale, bias, SiLU*up, residual, store or all-reduce push).
+//   warp 0      TMA producer: the packed weight tile [128 rows x 128 K]
+//               (64- or 128-byte swizzle), the activation tile [BN tokens x
+//               128 K] (128-byte swizzle, the MMA's B operand) and the stage's
+//               scale tables (group-128 scale/zero rows, or per-K scales) into
+//               a ring of shared-memory stages.  No multicast.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 with A read
+//               from tensor memory and B from shared memory, f32 accumulators in
+//               TMEM, 8 x K=16 per stage; tcgen05.commit releases the stages.
+//               For narrow token tiles the 8 MMAs of a stage rotate over up to
+//               four accumulators, so consecutive MMAs do not wait on each
+//               other's results; the epilogue adds the chains.
+//   warps 2..9  dequantizers, then the epilogue.  They form two groups of four
+//               warps (one warp per TMEM lane quarter); the groups take
+//               alternate stages, so two stages are dequantized at once.  Each
+//               thread owns one weight row of its stage: it reads the codes from
+//               shared memory, widens int4 pairs with one mask+or into the
+//               mantissas of an f16x2 (1024 + q), subtracts 1024 + zero exactly,
+//               applies the group scale (one f16 rounding, 2^-12 relative) and
+//               writes the f16 pairs straight into the TMEM A ring with
+//               tcgen05.st -- the dequantized operand never touches shared
+//               memory.  bf16 activation tiles are converted to f16 in place.
+//               Per work unit they then read the accumulator (tcgen05.ld) and
+//               run the epilogue: split-K reduction in split order, per-N /
+//               per-tensor scale, bias, SiLU*up, residual, store or all-reduce.
 //
 // Work units are (row tile, token tile, K split); CTAs loop over them.  A
-// split writes its f32 partial to the caller's workspace and the last split
-// to arrive (atomic ticket) sums all splits in split order, so results do not
-// depend on scheduling.  Every mbarrier wait is bounded by wall time; on
-// expiry the kernel records an error bit, drains its TMA copies and MMAs,
-// frees TMEM and returns.
+// split writes its f32 partial to the caller's workspace and the last split to
+// arrive (atomic ticket) sums all splits in split order, so results do not
+// depend on scheduling.  Every mbarrier wait is bounded (SM clock cycles); on
+// expiry the kernel records an error bit, drains its TMA copies and MMAs, frees
+// TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -41,18 +47,22 @@
 namespace ie {
 namespace tc {
 
-constexpr int kDqWarps = 8;     // dequant + epilogue warps (two per SM sub-partition)
+constexpr int kGroups = 2;      // dequant warp groups working on different sub-stages
+constexpr int kDqWarps = 4 * kGroups;
 constexpr int kDqThreads = kDqWarps * 32;
-constexpr int kThreads = 64 + kDqThreads;
+constexpr int kMmaWarps = 1;    // MMA issuing warps
+constexpr int kDqWarp0 = 1 + kMmaWarps;
+constexpr int kThreads = 32 * (kDqWarp0 + kDqWarps);
 constexpr int kTileN = 128;     // weight rows per tile = MMA M
 constexpr int kBK = 128;        // K per stage (one int4 group)
-constexpr int kMaxAStages = 4;  // dequantized A ring depth (4 for decode tiles, 2 for wide)
-constexpr int kABytes = kTileN * kBK * 2;   // one A stage (f16)
-constexpr uint64_t kWaitNs = 2000000000ull; // bounded mbarrier waits
+constexpr int kACols = kBK / 2; // TMEM columns of one A stage (two f16 per column)
+constexpr int kMaxAStages = 4;
+constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 2 GHz
+constexpr int kMinSmem = 120 * 1024;              // keeps one CTA per SM
 
 enum Fmt { F_INT4G = 0, F_INT4SYM = 1, F_INT8 = 2, F_FP8 = 3 };
 
-// error bits recorded by kernels of this file (read with ie_device_status)
+// error bits recorded by kernels of this file (read with ie_kernel_status)
 __device__ uint32_t g_tc_status = 0;
 constexpr uint32_t kErrWait = 1u;
 
@@ -60,9 +70,7 @@ struct TcParams {
   int64_t M, K, N;          // tokens, contraction, packed rows
   int axis, gate_up, epilogue, out_dtype;
   int x_bf16;               // activations arrive as bf16 and are converted to f16
-  const float* scale;       // per-K [K] / [2][K], per-N [N], per-tensor [1] / [2]
-  const __half* gscale;     // group-128 [K/128][N]
-  const __half* gzero;
+  const float* scale;       // per-N [N], per-tensor [1] / [2] (epilogue scales)
   const float* bias;
   const void* residual;
   int64_t ldr;
@@ -71,11 +79,17 @@ struct TcParams {
   int bn;                   // tokens per tile (MMA N)
   int n_tiles, m_tiles, splits, kstages;   // kstages = K / kBK
   int ns;                   // TMA ring depth
-  int na;                   // A ring depth
+  int na;                   // TMEM A ring depth
+  int acc_cols;             // TMEM columns of one accumulator chain
+  int chains;               // independent accumulator chains per issuer (1 or 2)
+  int issuers;              // MMA issuing threads (2 for tiles up to 128 tokens)
+  int tmem_cols;            // TMEM columns allocated
   int w_stage_bytes;        // packed weight bytes per stage
   int t_kind;               // stage tables: 0 none, 1 group s/z f16 [128] each, 2 per-K f32
   int t_rows;               // per-K tables: 1, or 2 for gate/up pairs
   int t_stage_bytes;        // table bytes per stage (1024-aligned slot)
+  int t_joint;              // group scale and zero tables are one [2][G][N] array
+  int sub;                  // 128-K sub-stages per TMA stage
   float* ws;                // split-K partials [splits][M][N]
   uint32_t* counters;       // per (m_tile, n_tile) tickets, self-resetting
 };
@@ -108,18 +122,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on an mbarrier phase; false (and an error bit) after kWaitNs.
+// Bounded wait on an mbarrier phase: false (and an error bit) once the SM
+// clock has advanced kWaitCycles, or at once if another role aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           const volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitNs) {
+    if (clock64() - t0 > kWaitCycles) {
       atomicOr(&g_tc_status, kErrWait);
       return false;
     }
+  }
+}
+// Unconditional bounded drain wait used at teardown.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity) && clock64() - t0 < kWaitCycles) {
   }
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
@@ -129,6 +150,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -147,29 +179,16 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
   asm volatile(
@@ -180,6 +199,32 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 32 consecutive TMEM columns of this thread's lane <- v[0..31]
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+// 16 consecutive TMEM columns of this thread's lane <- v[0..15]
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
@@ -194,114 +239,108 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, f32 accumulator, A/B of type ab (0 f16,
-// 1 bf16), both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t make_idesc(int ab, int n) {
-  return (1u << 4) | ((uint32_t)ab << 7) | ((uint32_t)ab << 10) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(kTileN >> 4) << 24);
+// Instruction descriptor: kind::f16, f32 accumulator, f16 A and B, both
+// K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t make_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTileN >> 4) << 24);
 }
 
-// Offset of the 16-byte chunk holding K elements [8j, 8j+8) of row r inside a
-// 64-wide SW128 K-major block (rows 128 bytes apart, chunks XOR-swizzled).
-__device__ __forceinline__ uint32_t sw128_offset(int r, int j) {
-  return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4));
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  return h2_bits(__floats2half2_rn(a, b));
 }
 
 // ---------------------------------------------------------------------------
-// dequantization of one 16-byte input chunk into A-operand chunks
+// dequantization of 32 K values of one row into 16 f16x2 words (TMEM columns)
 // ---------------------------------------------------------------------------
-template <typename TA> struct AType;
-template <> struct AType<__nv_bfloat16> {
-  static constexpr uint32_t kMagic = 0x43004300u;   // bf16x2 (128, 128)
-  static constexpr float kBias = 128.0f;
-  __device__ static uint32_t pack(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-  __device__ static uint32_t sub_mul(uint32_t v, uint32_t off, uint32_t s) {
-    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&v);
-    __nv_bfloat162 o = *reinterpret_cast<__nv_bfloat162*>(&off);
-    __nv_bfloat162 sc = *reinterpret_cast<__nv_bfloat162*>(&s);
-    __nv_bfloat162 r = __hmul2(__hsub2(x, o), sc);
-    return *reinterpret_cast<uint32_t*>(&r);
-  }
-  __device__ static uint32_t splat(float v) { return pack(v, v); }
-};
-template <> struct AType<__half> {
-  static constexpr uint32_t kMagic = 0x64006400u;   // f16x2 (1024, 1024)
-  static constexpr float kBias = 1024.0f;
-  __device__ static uint32_t pack(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-  __device__ static uint32_t sub_mul(uint32_t v, uint32_t off, uint32_t s) {
-    __half2 x = *reinterpret_cast<__half2*>(&v);
-    __half2 o = *reinterpret_cast<__half2*>(&off);
-    __half2 sc = *reinterpret_cast<__half2*>(&s);
-    __half2 r = __hmul2(__hsub2(x, o), sc);
-    return *reinterpret_cast<uint32_t*>(&r);
-  }
-  __device__ static uint32_t splat(float v) { return pack(v, v); }
-};
-
-__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
-  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(b & 0xFFu), __NV_E4M3);
-  return __half2float(__half(h));
-}
-
-// Dequantize one work item (row r of the tile, 16-byte input chunk c) of the
-// stage at K offset k0 into the A stage buffer `a` (two 64-wide SW128 blocks).
+// The sub-stage's packed row r lives at wst + r * row_bytes with its 16-byte
+// chunks XOR-swizzled by the TMA (64-byte swizzle for int4 rows: chunk ^
+// ((r>>1)&3); 128-byte swizzle for 8-bit rows: chunk ^ (r&7)), which keeps the 32
+// lanes of a warp -- 32 consecutive rows -- on distinct shared-memory banks.
+// q4 selects K values [32*q4, 32*q4 + 32) of the 128-wide sub-stage.
 template <int FMT>
-__device__ __forceinline__ void dequant_item(const TcParams& p, const uint8_t* wst, uint8_t* a,
-                                             int r, int c, int64_t n_row, const float* tbl,
-                                             uint32_t g_off, uint32_t g_scale) {
-  using AT = AType<__half>;
-  const int row_bytes = p.w_stage_bytes / kTileN;
-  const uint4 in = *reinterpret_cast<const uint4*>(wst + r * row_bytes + c * 16);
-  const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
-  if constexpr (FMT == F_INT4G) {
-    // 32 codes: K = c*32 .. c*32+31; one A chunk (8 values) per 32-bit word
+__device__ __forceinline__ void dequant_q4(const uint8_t* wst, int r, int q4, const uint8_t* tst,
+                                           int t_rows, int axis, int64_t n_row, int j_sub,
+                                           int sub, uint32_t (&o)[16]) {
+  if constexpr (FMT == F_INT4G || FMT == F_INT4SYM) {
+    const uint4 c = *reinterpret_cast<const uint4*>(wst + r * 64 + ((q4 ^ ((r >> 1) & 3)) << 4));
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    if constexpr (FMT == F_INT4G) {
+      // (1024 + q) - (1024 + z) is exact in f16; one rounding for * s.
+      // stage tables: [scale | zero][sub][128 rows] f16
+      const __half s = reinterpret_cast<const __half*>(tst)[j_sub * kTileN + r];
+      const __half z = reinterpret_cast<const __half*>(tst)[(sub + j_sub) * kTileN + r];
+      const __half2 off = __half2half2(__hadd(z, __float2half_rn(1024.0f)));
+      const __half2 sc = __half2half2(s);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t o[4];
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t t = ((w4[j] >> (4 * q)) & 0x000F000Fu) | AT::kMagic;
-        o[q] = AT::sub_mul(t, g_off, g_scale);
-      }
-      const int kk = c * 32 + 8 * j;
-      uint8_t* dst = a + (kk >> 6) * (kTileN * 128) + sw128_offset(r, (kk & 63) >> 3);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t t = ((w[j] >> (4 * q)) & 0x000F000Fu) | 0x64006400u;
+          o[4 * j + q] = h2_bits(__hmul2(__hsub2(bits_h2(t), off), sc));
+        }
+    } else {
+      // symmetric int4 stored q + 8: (1024 + q + 8) - 1032 = q exactly
+      const __half2 off = __half2half2(__float2half_rn(1032.0f));
+      // per-K tables: [rows][sub][128] f32
+      const float* sk = (axis == IE_AXIS_K)
+                            ? reinterpret_cast<const float*>(tst) +
+                                  ((t_rows == 2 ? (n_row & 1) : 0) * sub + j_sub) * kBK + 32 * q4
+                            : nullptr;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t t = ((w[j] >> (4 * q)) & 0x000F000Fu) | 0x64006400u;
+          const __half2 v = __hsub2(bits_h2(t), off);
+          if (sk) {
+            const float2 f = __half22float2(v);
+            o[4 * j + q] = pack_h2(f.x * sk[8 * j + 2 * q], f.y * sk[8 * j + 2 * q + 1]);
+          } else {
+            o[4 * j + q] = h2_bits(v);
+          }
+        }
     }
   } else {
-    // 8 or 32 codes per chunk; value per code in f32, then paired
-    constexpr int kPer = (FMT == F_INT4SYM) ? 32 : 16;
-    const int kbase = c * kPer;
-    const float* sk = nullptr;
-    if (p.axis == IE_AXIS_K) sk = tbl + (p.t_rows == 2 ? (n_row & 1) * kBK : 0) + kbase;
+    // 8-bit codes: 32 bytes = K values 32*q4 .. 32*q4+31
+    const uint8_t* row = wst + r * 128;
+    const int sw = r & 7;
+    uint32_t w[8];
 #pragma unroll
-    for (int j = 0; j < kPer / 8; ++j) {
-      float v[8];
+    for (int c = 0; c < 2; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(row + (((2 * q4 + c) ^ sw) << 4));
+      w[4 * c] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    const float* sk = (axis == IE_AXIS_K)
+                          ? reinterpret_cast<const float*>(tst) +
+                                ((t_rows == 2 ? (n_row & 1) : 0) * sub + j_sub) * kBK + 32 * q4
+                          : nullptr;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int idx = 8 * j + e;
-        float q;
-        if constexpr (FMT == F_INT4SYM) {
-          const uint32_t word = w4[idx >> 3];
-          const int pos = idx & 7;
-          const int nib = (pos & 1) ? 4 + (pos >> 1) : (pos >> 1);
-          q = (float)((word >> (4 * nib)) & 0xFu) - 8.0f;
-        } else if constexpr (FMT == F_INT8) {
-          q = (float)(int8_t)((w4[idx >> 2] >> (8 * (idx & 3))) & 0xFFu);
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const uint32_t pair = (w[j] >> (16 * q)) & 0xFFFFu;   // K = 4j+2q, 4j+2q+1
+        __half2 v;
+        if constexpr (FMT == F_INT8) {
+          // bytes as f16 1024 + (b ^ 0x80) = 1152 + q, exact; minus 1152 is exact
+          const uint32_t u = pair ^ 0x8080u;
+          const uint32_t t = (u & 0xFFu) | ((u & 0xFF00u) << 8) | 0x64006400u;
+          v = __hsub2(bits_h2(t), __half2half2(__float2half_rn(1152.0f)));
         } else {
-          q = e4m3_to_f32(w4[idx >> 2] >> (8 * (idx & 3)));
+          v = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)pair, __NV_E4M3));
         }
-        v[e] = sk ? q * sk[idx] : q;
+        if (sk) {
+          const float2 f = __half22float2(v);
+          const int k = 4 * j + 2 * q;
+          o[2 * j + q] = pack_h2(f.x * sk[k], f.y * sk[k + 1]);
+        } else {
+          o[2 * j + q] = h2_bits(v);
+        }
       }
-      const int kk = kbase + 8 * j;
-      uint8_t* dst = a + (kk >> 6) * (kTileN * 128) + sw128_offset(r, (kk & 63) >> 3);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(AT::pack(v[0], v[1]), AT::pack(v[2], v[3]),
-                                                  AT::pack(v[4], v[5]), AT::pack(v[6], v[7]));
     }
   }
 }
@@ -317,22 +356,49 @@ __device__ __forceinline__ float load_val(const void* in, int dt, int64_t i) {
   return static_cast<const float*>(in)[i];
 }
 
-// ---------------------------------------------------------------------------
-// the kernel
-// ---------------------------------------------------------------------------
 // bf16 -> f16 of one 16-byte chunk (8 values), in place.
 __device__ __forceinline__ void bf16_to_f16_chunk(uint4* p) {
   uint4 v = *p;
   uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float lo = __uint_as_float(w[i] << 16);
-    const float hi = __uint_as_float(w[i] & 0xFFFF0000u);
-    w[i] = AType<__half>::pack(lo, hi);
-  }
+  for (int i = 0; i < 4; ++i)
+    w[i] = pack_h2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
   *p = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Epilogue value of token m, row n, before the residual: scale, then bias.
+struct Epi {
+  const TcParams& p;
+  const ReduceCtx& rc;
+  uint32_t epoch;
+  int reduce;
+  // Writes one finished row value; gate/up pairs combine lanes (n even, n+1).
+  __device__ __forceinline__ void emit(int64_t m, int64_t n, float val, int lane) const {
+    if (p.epilogue & IE_EPI_SILU_MUL) {
+      if (p.epilogue & IE_EPI_BIAS) val += (n < p.N) ? p.bias[n] : 0.0f;
+      const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+      if ((lane & 1) == 0 && m < p.M && n + 1 < p.N) {
+        float o = (val / (1.0f + __expf(-val))) * partner;
+        const int64_t jcol = n >> 1;
+        if (p.epilogue & IE_EPI_RESIDUAL) o += load_val(p.residual, p.out_dtype, m * p.ldr + jcol);
+        store_val(p.out, p.out_dtype, m * p.ldo + jcol, o);
+      }
+    } else if (m < p.M && n < p.N) {
+      if (reduce) {
+        for (int dst = 0; dst < rc.world; ++dst)
+          landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + m * p.N + n] = val;
+      } else {
+        if (p.epilogue & IE_EPI_BIAS) val += p.bias[n];
+        if (p.epilogue & IE_EPI_RESIDUAL) val = load_val(p.residual, p.out_dtype, m * p.ldr + n) + val;
+        store_val(p.out, p.out_dtype, m * p.ldo + n, val);
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
@@ -341,110 +407,123 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int ns = p.ns, na = p.na;
-  const int x_stage_bytes = p.bn * kBK * 2;
-  uint8_t* a_ring = smem;                                   // na x 32 KB
-  uint8_t* x_ring = a_ring + na * kABytes;                  // ns x x_stage_bytes
+  const int ns = p.ns, na = p.na, sub = p.sub;
+  // one TMA stage = `sub` consecutive 128-K sub-stages behind one full/empty pair
+  const int w_sub_bytes = p.w_stage_bytes / sub;           // [128 rows][row bytes] per sub
+  const int x_sub_bytes = p.bn * kBK * 2;                    // two SW128 blocks per sub
+  const int x_stage_bytes = x_sub_bytes * sub;
+  uint8_t* x_ring = smem;                                   // ns x x_stage_bytes
   uint8_t* w_ring = x_ring + ns * x_stage_bytes;            // ns x w_stage_bytes
   uint8_t* t_ring = w_ring + ns * p.w_stage_bytes;          // ns x t_stage_bytes
   uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + ns * p.t_stage_bytes);
   uint64_t* full = bars;                 // [ns]  TMA landed (count 1 + tx)
-  uint64_t* empty = full + ns;           // [ns]  MMA done + dequant done (count 2)
-  uint64_t* afull = empty + ns;          // [na] dequant -> MMA (count 1)
-  uint64_t* aempty = afull + na;         // [na] MMA -> dequant (count 1)
-  uint64_t* accfull = aempty + na;       // MMA -> epilogue
+  uint64_t* empty = full + ns;           // [ns]  MMA done + every dequant warp done
+  uint64_t* afull = empty + ns;          // [na]  one group's four warps wrote A
+  uint64_t* aempty = afull + na;         // [na]  MMA read A (commit)
+  uint64_t* accfull = aempty + na;       // every issuer's MMAs of a unit done -> epilogue
   uint64_t* accempty = accfull + 1;      // epilogue -> MMA (count 1)
-  uint64_t* mma_done = accempty + 1;     // final commit: all MMAs retired
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* mma_done = accempty + 1;     // [kMmaWarps] final commits: all MMAs retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + kMmaWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(abort_flag) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tmem_cols = p.bn <= 32 ? 32 : (p.bn <= 64 ? 64 : (p.bn <= 128 ? 128 : 256));
   const uint32_t epoch = reduce ? reduce_epoch(rc) : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 2);
+      mbar_init(&empty[s], p.issuers + kDqWarps);   // each issuer's commit + every dequant warp
     }
     for (int s = 0; s < na; ++s) {
-      mbar_init(&afull[s], 1);
+      mbar_init(&afull[s], 4);
       mbar_init(&aempty[s], 1);
     }
-    mbar_init(accfull, 1);
+    mbar_init(accfull, p.issuers);
     mbar_init(accempty, 1);
-    mbar_init(mma_done, 1);
+    for (int i = 0; i < kMmaWarps; ++i) mbar_init(&mma_done[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(tmem_cols)
+                 "r"((uint32_t)p.tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // accumulators: issuer i, chain c at columns (i * chains + c) * acc_cols; A ring after them
   const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + (uint32_t)(p.acc_cols * p.chains * p.issuers);
 
+  // Work unit u = (row tile, token tile, K split).  Splits own whole TMA
+  // stages: sub-stages [ks0, ks1), ks0 a multiple of `sub`.
   const int units = p.n_tiles * p.m_tiles * p.splits;
+  const int tstages = (p.kstages + sub - 1) / sub;
   auto unit_range = [&](int u, int& nt, int& mt, int& ks0, int& ks1, int& sp) {
     nt = u % p.n_tiles;
     const int rest = u / p.n_tiles;
     mt = rest % p.m_tiles;
     sp = rest / p.m_tiles;
-    const int per = (p.kstages + p.splits - 1) / p.splits;
-    ks0 = sp * per;
-    ks1 = min(p.kstages, ks0 + per);
+    const int per = (tstages + p.splits - 1) / p.splits;
+    ks0 = sp * per * sub;
+    ks1 = min(p.kstages, ks0 + per * sub);
   };
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
-      int it = 0;
+      prefetch_tmap(&tm_w);
+      prefetch_tmap(&tm_x);
+      if (p.t_kind) prefetch_tmap(&tm_s);
+      if (p.t_kind == 1 && !p.t_joint) prefetch_tmap(&tm_z);
+      int ti = 0;
+      const uint32_t tbytes = p.t_kind == 1 ? (uint32_t)(2 * kTileN * 2 * sub)
+                              : (p.t_kind == 2 ? (uint32_t)(p.t_rows * kBK * 4 * sub) : 0u);
+      const int row_sub = w_sub_bytes / kTileN;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int nt, mt, ks0, ks1, sp;
         unit_range(u, nt, mt, ks0, ks1, sp);
-        for (int ks = ks0; ks < ks1; ++ks, ++it) {
-          const int s = it % ns;
-          if (!mbar_wait(&empty[s], ((it / ns) & 1) ^ 1, abort_flag)) {
+        for (int ks = ks0; ks < ks1; ks += sub, ++ti) {
+          const int s = ti % ns;
+          if (!mbar_wait(&empty[s], ((ti / ns) & 1) ^ 1, abort_flag)) {
             *abort_flag = 1;
             break;
           }
-          const uint32_t tbytes = p.t_kind == 1 ? 2 * kTileN * 2
-                                  : (p.t_kind == 2 ? (uint32_t)(p.t_rows * kBK * 4) : 0u);
           mbar_expect_tx(&full[s], (uint32_t)(p.w_stage_bytes + x_stage_bytes) + tbytes);
-          tma_load_2d(w_ring + s * p.w_stage_bytes, &tm_w, ks * (p.w_stage_bytes / kTileN),
-                      nt * kTileN, &full[s]);
+          uint8_t* ws_ = w_ring + s * p.w_stage_bytes;
+          for (int j = 0; j < sub; ++j)   // K past the end reads as zeros
+            tma_load_2d(ws_ + j * w_sub_bytes, &tm_w, (ks + j) * row_sub, nt * kTileN, &full[s]);
           uint8_t* ts = t_ring + s * p.t_stage_bytes;
           if (p.t_kind == 1) {
-            tma_load_2d(ts, &tm_s, nt * kTileN, ks, &full[s]);
-            tma_load_2d(ts + kTileN * 2, &tm_z, nt * kTileN, ks, &full[s]);
+            if (p.t_joint) {
+              tma_load_3d(ts, &tm_s, nt * kTileN, ks, 0, &full[s]);   // [s|z][sub][128]
+            } else {
+              tma_load_2d(ts, &tm_s, nt * kTileN, ks, &full[s]);
+              tma_load_2d(ts + sub * kTileN * 2, &tm_z, nt * kTileN, ks, &full[s]);
+            }
           } else if (p.t_kind == 2) {
-            tma_load_2d(ts, &tm_s, ks * kBK, 0, &full[s]);
+            tma_load_3d(ts, &tm_s, 0, ks, 0, &full[s]);               // [rows][sub][128]
           }
-          uint8_t* xs = x_ring + s * x_stage_bytes;
-          tma_load_2d(xs, &tm_x, ks * kBK, mt * p.bn, &full[s]);
-          tma_load_2d(xs + p.bn * 128, &tm_x, ks * kBK + 64, mt * p.bn, &full[s]);
+          // every 64-wide K block of the stage's activation tile in one copy
+          tma_load_3d(x_ring + s * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[s]);
         }
       }
       // drain: every issued stage's copy must have landed before exit
-      const int first = it > ns ? it - ns : 0;
-      for (int j = first; j < it; ++j) {
-        const int s = j % ns;
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[s], (j / ns) & 1) && globaltimer_ns() - t0 < kWaitNs) {
-        }
-      }
+      const int first = ti > ns ? ti - ns : 0;
+      for (int j = first; j < ti; ++j) mbar_drain(&full[j % ns], (j / ns) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------ MMA issuer --------------------------------
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc(0, p.bn);   // f16 x f16 -> f32
-      int it = 0, ait = 0, unit_i = 0;
+  } else if (warp <= kMmaWarps) {
+    // ------------------------------ MMA issuers -------------------------------
+    // issuer i takes the unit's sub-stages with local index % issuers == i
+    const int issuer = warp - 1;
+    if (lane == 0 && issuer < p.issuers) {
+      const uint32_t idesc = make_idesc(p.bn);
+      const uint32_t acc0 = tmem + (uint32_t)(issuer * p.chains * p.acc_cols);
+      int ti = 0, si = 0, unit_i = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
         int nt, mt, ks0, ks1, sp;
@@ -454,87 +533,103 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           break;
         }
         tc_fence_after();
-        for (int ks = ks0; ks < ks1; ++ks, ++it, ++ait) {
-          const int s = it % ns, a = ait % na;
-          if (!mbar_wait(&full[s], (it / ns) & 1, abort_flag) ||
-              !mbar_wait(&afull[a], (ait / na) & 1, abort_flag)) {
+        bool fresh = true;
+        for (int ks = ks0; ks < ks1 && ok; ks += sub, ++ti) {
+          const int s = ti % ns;
+          const int nsub = min(sub, ks1 - ks);
+          const uint32_t x_stage = smem_u32(x_ring + s * x_stage_bytes);
+          // Every role that arrives on empty[s] first waits for this use of the
+          // stage to land, so no arrival can be credited to an earlier phase.
+          if (!mbar_wait(&full[s], (ti / ns) & 1, abort_flag)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(a_ring + a * kABytes);
-          const uint32_t x_base = smem_u32(x_ring + s * x_stage_bytes);
-#pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_desc(a_base + kb * (kTileN * 128) + kk * 32);
-              const uint64_t bd = sw128_desc(x_base + kb * (p.bn * 128) + kk * 32);
-              tc_mma(tmem, ad, bd, idesc, (ks > ks0 || kb > 0 || kk > 0) ? 1u : 0u);
+          for (int j = 0; j < nsub; ++j, ++si) {
+            if ((ks - ks0 + j) % p.issuers != issuer) continue;
+            const int a = si % na;
+            // afull implies the stage's TMA landed: the dequant warps waited on it
+            if (!mbar_wait(&afull[a], (si / na) & 1, abort_flag)) {
+              ok = false;
+              break;
             }
-          tc_commit(&empty[s]);
-          tc_commit(&aempty[a]);
+            tc_fence_after();
+            const uint32_t a_col = tmem_a + (uint32_t)(a * kACols);
+            const uint32_t x_base = x_stage + (uint32_t)(j * x_sub_bytes);
+            const int chains = p.chains;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t bd = sw128_desc(x_base + (kk >> 2) * (p.bn * 128) + (kk & 3) * 32);
+              const int c = kk & (chains - 1);
+              tc_mma_ts(acc0 + (uint32_t)(c * p.acc_cols), a_col + (uint32_t)(kk * 8), bd, idesc,
+                        (!fresh || kk >= chains) ? 1u : 0u);
+            }
+            fresh = false;
+            tc_commit(&aempty[a]);
+          }
+          if (ok) tc_commit(&empty[s]);
         }
         if (!ok) break;
         tc_commit(accfull);
       }
       if (!ok) *abort_flag = 1;
       // every MMA this thread issued must finish before TMEM is released
-      tc_commit(mma_done);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(mma_done, 0) && globaltimer_ns() - t0 < kWaitNs) {
-      }
+      tc_commit(&mma_done[issuer]);
+      mbar_drain(&mma_done[issuer], 0);
     }
   } else {
-    // ---------------------- dequantize + epilogue (256 threads) ----------------------
-    const int dt = threadIdx.x - 64;
+    // ---------------------- dequantize + epilogue ----------------------
+    const int dt = threadIdx.x - 32 * kDqWarp0;   // 0 .. kDqThreads-1
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter ..
-    const int half = (warp - 2) >> 2;             // which half of the columns
-    const int row = quarter * 32 + lane;          // accumulator row of this thread
-    constexpr int kChunks = (FMT == F_INT4G || FMT == F_INT4SYM) ? 4 : 8;  // per row per stage
-    constexpr int kItems = kTileN * kChunks / kDqThreads;                  // per thread
-    int it = 0, ait = 0, unit_i = 0;
+    const int group = (warp - kDqWarp0) >> 2;     // which sub-stages this warp dequantizes
+    const int gt = dt & 127;                      // thread index within the group
+    const int row = quarter * 32 + lane;          // weight row = accumulator lane
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    int ti = 0, si = 0, unit_i = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
-      for (int ks = ks0; ks < ks1; ++ks, ++it, ++ait) {
-        const int s = it % ns, a = ait % na;
-        if (!mbar_wait(&full[s], (it / ns) & 1, abort_flag) ||
-            !mbar_wait(&aempty[a], ((ait / na) & 1) ^ 1, abort_flag)) {
+      const int64_t n = (int64_t)nt * kTileN + row;
+      for (int ks = ks0; ks < ks1 && ok; ks += sub, ++ti) {
+        const int s = ti % ns;
+        const int nsub = min(sub, ks1 - ks);
+        // wait for this use of the stage even without a sub-stage to dequantize:
+        // the arrival on empty[s] below must not run ahead of the producer
+        if (!mbar_wait(&full[s], (ti / ns) & 1, abort_flag)) {
           ok = false;
           break;
         }
-        const uint8_t* wst = w_ring + s * p.w_stage_bytes;
-        uint8_t* ast = a_ring + a * kABytes;
-        const uint8_t* tst = t_ring + s * p.t_stage_bytes;
-#pragma unroll
-        for (int i = 0; i < kItems; ++i) {
-          const int item = dt + i * kDqThreads;
-          const int r = item / kChunks, c = item % kChunks;
-          const int64_t n_row = (int64_t)nt * kTileN + r;
-          uint32_t g_off = 0, g_scale = 0;
-          if constexpr (FMT == F_INT4G) {
-            // rows past N were zero-filled by the TMA, so s = 0 there
-            const __half s_ = reinterpret_cast<const __half*>(tst)[r];
-            const __half z_ = reinterpret_cast<const __half*>(tst + kTileN * 2)[r];
-            const __half zb = __hadd(z_, __float2half_rn(AType<__half>::kBias));
-            g_off = (uint32_t)__half_as_ushort(zb) * 0x10001u;
-            g_scale = (uint32_t)__half_as_ushort(s_) * 0x10001u;
+        for (int j = 0; j < nsub; ++j, ++si) {
+          if ((ks - ks0 + j) % kGroups != group) continue;   // another group takes it
+          const int a = si % na;
+          if (!mbar_wait(&aempty[a], ((si / na) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
           }
-          dequant_item<FMT>(p, wst, ast, r, c, n_row, reinterpret_cast<const float*>(tst),
-                            g_off, g_scale);
+          const uint8_t* wst = w_ring + s * p.w_stage_bytes + j * w_sub_bytes;
+          const uint8_t* tst = t_ring + s * p.t_stage_bytes;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            uint32_t o[32];
+            uint32_t (&lo)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[0]);
+            uint32_t (&hi)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[16]);
+            dequant_q4<FMT>(wst, row, 2 * h, tst, p.t_rows, p.axis, n, j, sub, lo);
+            dequant_q4<FMT>(wst, row, 2 * h + 1, tst, p.t_rows, p.axis, n, j, sub, hi);
+            tmem_st32(tmem_a + lane_addr + (uint32_t)(a * kACols + h * 32), o);
+          }
+          if (p.x_bf16) {
+            uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
+            for (int i = gt; i < x_sub_bytes / 16; i += 128) bf16_to_f16_chunk(xs + i);
+            fence_proxy_async();
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[a]);
         }
-        if (p.x_bf16) {
-          uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes);
-          for (int i = dt; i < x_stage_bytes / 16; i += kDqThreads) bf16_to_f16_chunk(xs + i);
-        }
-        fence_proxy_async();
-        named_sync(1, kDqThreads);
-        if (dt == 0) {
-          mbar_arrive(&afull[a]);
-          mbar_arrive(&empty[s]);
-        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);   // this warp is done with the stage
       }
       if (!ok) break;
 
@@ -544,7 +639,6 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         break;
       }
       tc_fence_after();
-      const int64_t n = (int64_t)nt * kTileN + row;
       const int64_t m0 = (int64_t)mt * p.bn;
       const bool split = p.splits > 1;
       float nscale = 1.0f;
@@ -552,44 +646,26 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         if (p.axis == IE_AXIS_N) nscale = p.scale[n];
         else if (p.axis == IE_AXIS_TENSOR) nscale = p.scale[p.gate_up ? (n & 1) : 0];
       }
-      // pass 1: TMEM -> registers -> (workspace | final); this warp owns the
-      // columns [c_lo, c_hi) of its lane quarter
-      const int c_lo = half * (p.bn / 2), c_hi = c_lo + p.bn / 2;
-      for (int c0 = c_lo; c0 < c_hi; c0 += 8) {
+      const Epi epi{p, rc, epoch, reduce};
+      // accumulators holding this unit: issuers that took at least one sub-stage
+      const int nacc = p.chains * min(p.issuers, ks1 - ks0);
+      // this warp owns the 8-token column chunks c0 = 8 * (group + kGroups * i)
+      for (int c0 = 8 * group; c0 < p.bn; c0 += 8 * kGroups) {
         float v[8];
-        tmem_ld8(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
-        if (split) {
+        tmem_ld8(tmem + lane_addr + (uint32_t)c0, v);
+        for (int c = 1; c < nacc; ++c) {
+          float w[8];
+          tmem_ld8(tmem + lane_addr + (uint32_t)(c * p.acc_cols + c0), w);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int64_t m = m0 + c0 + j;
+          for (int j = 0; j < 8; ++j) v[j] += w[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int64_t m = m0 + c0 + j;
+          if (split) {
             if (m < p.M && n < p.N) p.ws[((int64_t)sp * p.M + m) * p.N + n] = v[j];
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            // finalize token m0+c0+j for row n
-            const int64_t m = m0 + c0 + j;
-            float val = v[j] * nscale;
-            if (p.epilogue & IE_EPI_SILU_MUL) {
-              if (p.epilogue & IE_EPI_BIAS) val += (n < p.N) ? p.bias[n] : 0.0f;
-              const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
-              if ((lane & 1) == 0 && m < p.M && n + 1 < p.N) {
-                float o = (val / (1.0f + __expf(-val))) * partner;
-                const int64_t jcol = n >> 1;
-                if (p.epilogue & IE_EPI_RESIDUAL) o += load_val(p.residual, p.out_dtype, m * p.ldr + jcol);
-                store_val(p.out, p.out_dtype, m * p.ldo + jcol, o);
-              }
-            } else if (m < p.M && n < p.N) {
-              if (reduce) {
-                for (int dst = 0; dst < rc.world; ++dst)
-                  landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + m * p.N + n] = val;
-              } else {
-                if (p.epilogue & IE_EPI_BIAS) val += p.bias[n];
-                if (p.epilogue & IE_EPI_RESIDUAL)
-                  val = load_val(p.residual, p.out_dtype, m * p.ldr + n) + val;
-                store_val(p.out, p.out_dtype, m * p.ldo + n, val);
-              }
-            }
+          } else {
+            epi.emit(m, n, v[j] * nscale, lane);
           }
         }
       }
@@ -611,7 +687,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         finalize_here = *s_ticket != 0;
         if (finalize_here) {
           __threadfence();
-          for (int j = c_lo; j < c_hi; ++j) {
+          for (int j = 0; j < p.bn; ++j) {
+            if (((j >> 3) % kGroups) != group) continue;   // same column ownership as above
             const int64_t m = m0 + j;
             float acc = 0.0f;
             if (m < p.M && n < p.N) {
@@ -619,27 +696,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
               for (int q = 1; q < p.splits; ++q)
                 acc += __ldcg(p.ws + ((int64_t)q * p.M + m) * p.N + n);
             }
-            float val = acc * nscale;
-            if (p.epilogue & IE_EPI_SILU_MUL) {
-              if (p.epilogue & IE_EPI_BIAS) val += (n < p.N) ? p.bias[n] : 0.0f;
-              const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
-              if ((lane & 1) == 0 && m < p.M && n + 1 < p.N) {
-                float o = (val / (1.0f + __expf(-val))) * partner;
-                const int64_t jcol = n >> 1;
-                if (p.epilogue & IE_EPI_RESIDUAL) o += load_val(p.residual, p.out_dtype, m * p.ldr + jcol);
-                store_val(p.out, p.out_dtype, m * p.ldo + jcol, o);
-              }
-            } else if (m < p.M && n < p.N) {
-              if (reduce) {
-                for (int dst = 0; dst < rc.world; ++dst)
-                  landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + m * p.N + n] = val;
-              } else {
-                if (p.epilogue & IE_EPI_BIAS) val += p.bias[n];
-                if (p.epilogue & IE_EPI_RESIDUAL)
-                  val = load_val(p.residual, p.out_dtype, m * p.ldr + n) + val;
-                store_val(p.out, p.out_dtype, m * p.ldo + n, val);
-              }
-            }
+            epi.emit(m, n, acc * nscale, lane);
           }
           if (dt == 0) p.counters[tile_id] = 0u;
         }
@@ -661,7 +718,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(tmem_cols)
+                 "r"((uint32_t)p.tmem_cols)
                  : "memory");
   }
 
@@ -722,6 +779,7 @@ EncodeFn encode_fn() {
 
 struct Plan {
   int fmt = 0, bn = 16, m_tiles = 1, n_tiles = 1, splits = 1, kstages = 1, ns = 2, na = 2;
+  int acc_cols = 32, chains = 1, issuers = 1, tmem_cols = 512, sub = 1;
   int w_stage_bytes = 0;
   int t_kind = 0, t_rows = 0, t_stage_bytes = 0;
   size_t smem = 0;
@@ -758,16 +816,22 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   pl.n_tiles = (int)((a.w.n + kTileN - 1) / kTileN);
   pl.kstages = (int)(a.w.k / kBK);
   const int row_stage = (pl.fmt == F_INT4G || pl.fmt == F_INT4SYM) ? kBK / 2 : kBK;
-  pl.w_stage_bytes = row_stage * kTileN;
+  // a TMA stage carries 32 KB of weights (4 int4 groups or 2 8-bit ones) when the
+  // token tile leaves room: large stages amortise the barrier round trips
+  pl.sub = row_stage == kBK / 2 ? 4 : 2;
+  while (pl.sub > 1 && (size_t)pl.sub * (row_stage * kTileN + pl.bn * kBK * 2) > 100 * 1024)
+    pl.sub /= 2;
+  pl.w_stage_bytes = row_stage * kTileN * pl.sub;
   const int sms = sm_count();
   const double wbytes = (double)a.w.n * a.w.k * (row_stage / (double)kBK);
   double best = -1.0;
   const int tiles = pl.n_tiles * pl.m_tiles;
+  const int tst = (pl.kstages + pl.sub - 1) / pl.sub;   // TMA stages along K
   for (int s = 1; s <= (allow_split ? 16 : 1); ++s) {
-    if (s > 1 && pl.kstages < 2 * s) break;
-    // every split must own at least one stage: (s-1) * ceil(kstages/s) < kstages
-    const int per = (pl.kstages + s - 1) / s;
-    if ((s - 1) * per >= pl.kstages) continue;
+    if (s > 1 && tst < 2 * s) break;
+    // every split must own at least one TMA stage: (s-1) * ceil(tst/s) < tst
+    const int per = (tst + s - 1) / s;
+    if ((s - 1) * per >= tst) continue;
     const int units = tiles * s;
     const int waves = (units + sms - 1) / sms;
     const double eff = (double)units / ((double)waves * sms);
@@ -780,20 +844,31 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   }
   if (a.w.axis == IE_AXIS_GROUP128) {
     pl.t_kind = 1;
-    pl.t_stage_bytes = 1024;
+    pl.t_stage_bytes = ((2 * kTileN * 2 * pl.sub + 1023) / 1024) * 1024;
   } else if (a.w.axis == IE_AXIS_K) {
     pl.t_kind = 2;
     pl.t_rows = a.w.gate_up ? 2 : 1;
-    pl.t_stage_bytes = 1024;
+    pl.t_stage_bytes = ((pl.t_rows * kBK * 4 * pl.sub + 1023) / 1024) * 1024;
   }
-  const size_t x_stage = (size_t)pl.bn * kBK * 2;
+  // TMEM: accumulator columns (power of two >= 32) then the A ring, 64 columns a stage
+  // narrow tiles rotate their MMAs over independent accumulator chains and two
+  // issuing threads (one tcgen05.mma M=128 K=16 costs ~50 cycles to issue, and
+  // two issuers overlap)
+  pl.acc_cols = ((pl.bn + 15) / 16) * 16;
+  pl.issuers = 1;
+  pl.chains = pl.bn <= 32 ? 4 : (pl.bn <= 64 ? 2 : 1);
+  const int accs = pl.acc_cols * pl.chains * pl.issuers;
+  pl.na = (accs + kMaxAStages * kACols <= 512) ? kMaxAStages : 2;
+  pl.tmem_cols = 32;
+  while (pl.tmem_cols < accs + pl.na * kACols) pl.tmem_cols *= 2;
+  const size_t x_stage = (size_t)pl.bn * kBK * 2 * pl.sub;
   const size_t budget = 220 * 1024;
-  pl.na = pl.bn <= 64 ? kMaxAStages : 2;
-  const size_t fixed = (size_t)pl.na * kABytes + 1024 + 256;
+  const size_t fixed = 1024 + 256;
   const size_t per = x_stage + pl.w_stage_bytes + pl.t_stage_bytes;
-  pl.ns = (int)std::min<size_t>(8, (budget - fixed) / per);
+  pl.ns = (int)std::min<size_t>(12, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
-  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 3) + 16;
+  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps) + 16;
+  if (pl.smem < (size_t)kMinSmem) pl.smem = kMinSmem;   // one CTA per SM: TMEM and co-residency
   if (pl.splits > 1) {
     pl.counters_bytes = (((size_t)tiles * 4) + 255) / 256 * 256;
     pl.ws_bytes = pl.counters_bytes + (size_t)pl.splits * M * a.w.n * 4;
@@ -851,30 +926,48 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
     const cuuint64_t row_bytes = (cuuint64_t)(a.w.format == IE_FMT_INT4 ? a.w.k / 2 : a.w.k);
     const cuuint64_t dims[2] = {row_bytes, (cuuint64_t)a.w.n};
     const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)(pl.w_stage_bytes / kTileN), (cuuint32_t)kTileN};
+    const int row_sub = pl.w_stage_bytes / pl.sub / kTileN;   // bytes of one row per sub-stage
+    const cuuint32_t box[2] = {(cuuint32_t)row_sub, (cuuint32_t)kTileN};
     const cuuint32_t estr[2] = {1, 1};
+    // 64-byte int4 rows use the 64-byte swizzle, 128-byte 8-bit rows the 128-byte one,
+    // so the dequant threads (one row each) read distinct banks
+    const CUtensorMapSwizzle sw = row_sub == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B;
     CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a.w.codes), dims,
-                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(weights): %d", (int)r);
   }
   {
-    const cuuint64_t dims[2] = {(cuuint64_t)a.w.k, (cuuint64_t)a.m};
-    const cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)pl.bn};
-    const cuuint32_t estr[2] = {1, 1};
+    // x viewed as [K/64][M][64]: one box {64, BN, 2} is a stage's two SW128 blocks
+    const cuuint64_t dims[3] = {64, (cuuint64_t)a.m, (cuuint64_t)(a.w.k / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)a.ldx * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)pl.bn, (cuuint32_t)(2 * pl.sub)};
+    const cuuint32_t estr[3] = {1, 1, 1};
     const CUtensorMapDataType dt = a.act_dtype == IE_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUresult r = enc(&tx, dt, 2, const_cast<void*>(a.x), dims, strides, box, estr,
+    CUresult r = enc(&tx, dt, 3, const_cast<void*>(a.x), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(x): %d", (int)r);
   }
   CUtensorMap ts = tw, tz = tw;   // unused copies when the stage carries no tables
-  if (pl.t_kind == 1) {
+  const bool joint = pl.t_kind == 1 &&
+                     static_cast<const char*>(a.w.zero) ==
+                         static_cast<const char*>(a.w.scale) + (a.w.k / 128) * a.w.n * 2;
+  if (joint) {
+    const cuuint64_t dims[3] = {(cuuint64_t)a.w.n, (cuuint64_t)(a.w.k / 128), 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)a.w.n * 2, (cuuint64_t)(a.w.k / 128) * a.w.n * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kTileN, (cuuint32_t)pl.sub, 2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(a.w.scale), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(tables): %d", (int)r);
+  } else if (pl.t_kind == 1) {
     const cuuint64_t dims[2] = {(cuuint64_t)a.w.n, (cuuint64_t)(a.w.k / 128)};
     const cuuint64_t strides[1] = {(cuuint64_t)a.w.n * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kTileN, 1};
+    const cuuint32_t box[2] = {(cuuint32_t)kTileN, (cuuint32_t)pl.sub};
     const cuuint32_t estr[2] = {1, 1};
     for (int i = 0; i < 2; ++i) {
       CUresult r = enc(i ? &tz : &ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
@@ -884,11 +977,12 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
       if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(groups): %d", (int)r);
     }
   } else if (pl.t_kind == 2) {
-    const cuuint64_t dims[2] = {(cuuint64_t)a.w.k, (cuuint64_t)pl.t_rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)a.w.k * 4};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)pl.t_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(a.w.scale), dims,
+    // per-K scales viewed as [rows][K/128][128]
+    const cuuint64_t dims[3] = {(cuuint64_t)kBK, (cuuint64_t)(a.w.k / kBK), (cuuint64_t)pl.t_rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)kBK * 4, (cuuint64_t)a.w.k * 4};
+    const cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)pl.sub, (cuuint32_t)pl.t_rows};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(a.w.scale), dims,
                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(k scales): %d", (int)r);
@@ -901,12 +995,7 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   prm.gate_up = a.w.gate_up;
   prm.epilogue = a.epilogue;
   prm.out_dtype = a.out_dtype;
-  if (a.w.axis == IE_AXIS_GROUP128) {
-    prm.gscale = static_cast<const __half*>(a.w.scale);
-    prm.gzero = static_cast<const __half*>(a.w.zero);
-  } else {
-    prm.scale = static_cast<const float*>(a.w.scale);
-  }
+  if (a.w.axis != IE_AXIS_GROUP128) prm.scale = static_cast<const float*>(a.w.scale);
   prm.bias = a.bias;
   prm.residual = a.residual;
   prm.ldr = a.ldr;
@@ -919,10 +1008,16 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   prm.kstages = pl.kstages;
   prm.ns = pl.ns;
   prm.na = pl.na;
+  prm.acc_cols = pl.acc_cols;
+  prm.chains = pl.chains;
+  prm.issuers = pl.issuers;
+  prm.tmem_cols = pl.tmem_cols;
   prm.w_stage_bytes = pl.w_stage_bytes;
   prm.t_kind = pl.t_kind;
   prm.t_rows = pl.t_rows;
   prm.t_stage_bytes = pl.t_stage_bytes;
+  prm.t_joint = joint ? 1 : 0;
+  prm.sub = pl.sub;
   if (pl.splits > 1) {
     prm.counters = static_cast<uint32_t*>(a.workspace);
     prm.ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pl.counters_bytes);

@@ -28,6 +28,16 @@ _AXIS_NAMES = {_lib.IE_AXIS_K: "k", _lib.IE_AXIS_N: "n", _lib.IE_AXIS_TENSOR: "t
                _lib.IE_AXIS_GROUP128: "group128"}
 
 
+def _adjacent(scale, zero) -> bool:
+    return (scale.is_contiguous() and zero.is_contiguous() and scale.shape == zero.shape
+            and zero.data_ptr() == scale.data_ptr() + scale.numel() * scale.element_size())
+
+
+def torch_empty_like_pair(t):
+    torch = require_cuda()
+    return torch.empty((2,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+
+
 class PackedWeight:
     """A quantized ``[K, N]`` weight resident in device memory."""
 
@@ -38,6 +48,13 @@ class PackedWeight:
         self.k = int(k)
         self.n = int(n)
         self.codes = codes
+        if zero is not None and scale.dim() == 2 and not _adjacent(scale, zero):
+            # group tables live in one [2][G][N] array (scale, then zero) so the
+            # tensor-core kernel fetches both with a single copy per stage
+            joint = torch_empty_like_pair(scale)
+            joint[0].copy_(scale)
+            joint[1].copy_(zero)
+            scale, zero = joint[0], joint[1]
         self.scale = scale
         self.zero = zero
         self.int4_symmetric = bool(int4_symmetric)
