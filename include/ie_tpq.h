@@ -150,6 +150,23 @@ int ie_dequantize(const ie_qweight* w, int32_t layout, int32_t out_dtype, void* 
  * holds tickets that must be zero before first use and are left zero. */
 size_t ie_qlinear_workspace_size(const ie_qlinear_args* a);
 int ie_qlinear(const ie_qlinear_args* a, void* stream);
+
+/* ---- quantized linear that allocates nothing ----------------------------------
+ * No counterpart in the reference (whose linear layers are CPU numpy): an
+ * addition for callers that cannot allocate device memory at call time -- work
+ * recorded into a CUDA graph with a fixed memory plan, or an engine whose
+ * allocator owns all of HBM -- yet want the split-K tensor-core kernel.
+ * Same arguments and result as ie_qlinear on the tensor-core path; workspace
+ * and workspace_bytes are ignored.  The split-K partials and tile tickets live
+ * in a static device array of IE_QLINEAR_NOALLOC_SCRATCH_BYTES inside the
+ * library; a call whose plan needs more returns IE_ERR_INVALID, and a call the
+ * tensor-core kernel cannot serve (f32 activations, K % 128 != 0, unaligned
+ * rows, algo 1) returns IE_ERR_UNSUPPORTED.  The first call on a device looks
+ * up that device's copy of the array (cudaGetSymbolAddress, which may load the
+ * module): make it before any stream capture.  The array is shared by all calls
+ * on a device, so calls that overlap on the GPU (concurrent streams) race. */
+#define IE_QLINEAR_NOALLOC_SCRATCH_BYTES (8u << 20)
+int ie_qlinear_noalloc(const ie_qlinear_args* a, void* stream);
 /* Error bits recorded by kernels (1 = a bounded pipeline wait expired);
  * synchronous read of device state, optionally cleared. */
 int ie_kernel_status(uint32_t* bits, int32_t clear);

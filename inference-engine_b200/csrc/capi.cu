@@ -89,6 +89,13 @@ extern "C" int ie_qlinear(const ie_qlinear_args* a, void* stream) {
   return launch_qlinear_gemv(*a, nullptr, 0, as_stream(stream));
 }
 
+extern "C" int ie_qlinear_noalloc(const ie_qlinear_args* a, void* stream) {
+  IE_CHECK(a, "qlinear_noalloc: null args");
+  int rc = validate_linear(*a);
+  if (rc) return rc;
+  return launch_qlinear_tc_static(*a, as_stream(stream));
+}
+
 extern "C" int ie_kernel_status(uint32_t* bits, int32_t clear) {
   IE_CHECK(bits, "kernel_status: null output");
   *bits = tc_read_status(clear != 0);

@@ -145,6 +145,9 @@ size_t tc_workspace_bytes(const ie_qlinear_args& a);
 int64_t tc_tiles(const ie_qlinear_args& a);
 int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_t s);
 uint32_t tc_read_status(bool clear);
+// The tensor-core call with its split-K scratch in the library's static device
+// array instead of a caller workspace (ie_qlinear_noalloc); allocates nothing.
+int launch_qlinear_tc_static(const ie_qlinear_args& a, cudaStream_t s);
 // Fills rc for a collective call of comm c after checking its limits.
 int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_rank);
 

@@ -1031,6 +1031,73 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Static split-K scratch (ie_qlinear_noalloc).  Callers that may not allocate
+// device memory -- code recorded into a CUDA graph whose memory plan is fixed,
+// an engine whose allocator owns every byte of HBM, a real-time decode loop --
+// still need somewhere for the f32 split-K partials and tile tickets.  This
+// array is part of the module image: the driver reserves it on each device
+// when the module loads, so using it never allocates.  It is shared by every
+// call on a device: two such calls overlapping on the GPU (different streams,
+// or threads without ordering between them) race on the partials and tickets.
+namespace tc {
+
+static_assert(IE_QLINEAR_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size");
+static __device__ __align__(256) unsigned char g_static_scratch[IE_QLINEAR_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_scratch_once[kMaxDevices];
+void* g_scratch_ptr[kMaxDevices];
+cudaError_t g_scratch_err[kMaxDevices];
+
+// Device address of this device's copy of the array, looked up once per device
+// with that device current (the look-up may load the module, which is why the
+// first call on a device belongs before any stream capture).
+int static_scratch(void** out) {
+  int dev = 0;
+  IE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(IE_ERR_UNSUPPORTED, "qlinear_noalloc: device ordinal %d >= %d", dev,
+                     kMaxDevices);
+  std::call_once(g_scratch_once[dev], [dev] {
+    void* p = nullptr;
+    g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_static_scratch);
+    g_scratch_ptr[dev] = g_scratch_err[dev] == cudaSuccess ? p : nullptr;
+  });
+  if (g_scratch_err[dev] != cudaSuccess)
+    return set_error(IE_ERR_CUDA, "qlinear_noalloc: cudaGetSymbolAddress(scratch) on device %d: %s",
+                     dev, cudaGetErrorString(g_scratch_err[dev]));
+  *out = g_scratch_ptr[dev];
+  return IE_OK;
+}
+
+}  // namespace tc
+
+int launch_qlinear_tc_static(const ie_qlinear_args& a, cudaStream_t s) {
+  using namespace tc;
+  void* scratch = nullptr;
+  int rc = static_scratch(&scratch);
+  if (rc || a.m == 0) return rc;
+  if (a.algo == 1 || !tc_eligible(a))
+    return set_error(IE_ERR_UNSUPPORTED,
+                     "qlinear_noalloc: only the tensor-core path is served (bf16/f16 "
+                     "activations, K %% 128 == 0, 16-byte aligned rows, algo 0 or 2)");
+  const Plan pl = make_plan(a, true);
+  if (pl.ws_bytes > IE_QLINEAR_NOALLOC_SCRATCH_BYTES)
+    return set_error(IE_ERR_INVALID,
+                     "qlinear_noalloc: %lld tokens x %lld rows need %zu bytes of split-K "
+                     "scratch; the static scratch holds %zu (use ie_qlinear with a workspace)",
+                     (long long)a.m, (long long)a.w.n, pl.ws_bytes,
+                     (size_t)IE_QLINEAR_NOALLOC_SCRATCH_BYTES);
+  ie_qlinear_args b = a;
+  b.workspace = scratch;
+  b.workspace_bytes = IE_QLINEAR_NOALLOC_SCRATCH_BYTES;
+  // tickets must read zero when the kernel starts; a call that ended early on an
+  // expired wait may have left some set
+  if (pl.splits > 1) IE_CUDA_TRY(cudaMemsetAsync(scratch, 0, pl.counters_bytes, s));
+  return launch_qlinear_tc(b, nullptr, s);
+}
+
 uint32_t tc_read_status(bool clear) {
   uint32_t v = 0;
   cudaMemcpyFromSymbol(&v, tc::g_tc_status, sizeof(v));

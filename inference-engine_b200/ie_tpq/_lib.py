@@ -40,12 +40,14 @@ IE_EPI_RESIDUAL = 2
 IE_EPI_SILU_MUL = 4
 
 IE_COMM_HANDLE_BYTES = 64
+IE_QLINEAR_NOALLOC_SCRATCH_BYTES = 8 << 20
 
 # every symbol include/ie_tpq.h declares
 EXPORTED = (
     "ie_version", "ie_last_error", "ie_quantize_integer", "ie_quantize_float",
     "ie_round_to_float_format", "ie_pack_weight", "ie_dequantize",
-    "ie_qlinear_workspace_size", "ie_qlinear", "ie_kernel_status", "ie_rms_norm",
+    "ie_qlinear_workspace_size", "ie_qlinear", "ie_qlinear_noalloc", "ie_kernel_status",
+    "ie_rms_norm",
     "ie_reduce_partials", "ie_comm_create",
     "ie_comm_export", "ie_comm_open", "ie_comm_destroy", "ie_comm_set_timeout",
     "ie_comm_check", "ie_qlinear_allreduce", "ie_allreduce",
@@ -106,6 +108,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "ie_dequantize": (ctypes.c_int, [ctypes.POINTER(QWeight), _I32, _I32, _P, _P]),
         "ie_qlinear_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(QLinearArgs)]),
         "ie_qlinear": (ctypes.c_int, [ctypes.POINTER(QLinearArgs), _P]),
+        "ie_qlinear_noalloc": (ctypes.c_int, [ctypes.POINTER(QLinearArgs), _P]),
         "ie_kernel_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _I32]),
         "ie_rms_norm": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _I64, _I32, _I64, _I64,
                                        ctypes.c_float, _P]),
