@@ -3,20 +3,22 @@
 //
 // The weight is the MMA's A operand (M = 128 output rows per tile) and the
 // token batch is its N dimension (16..256), so decode batches and prefill
-// batches use the same kernel.  Per CTA (320 threads, one CTA per SM):
+// batches use the same kernel.  Per CTA (352 threads, one CTA per SM):
 //
 //   warp 0      TMA producer: the packed weight tile [128 rows x 128 K]
 //               (64- or 128-byte swizzle), the activation tile [BN tokens x
 //               128 K] (128-byte swizzle, the MMA's B operand) and the stage's
 //               scale tables (group-128 scale/zero rows, or per-K scales) into
 //               a ring of shared-memory stages.  No multicast.
-//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 with A read
-//               from tensor memory and B from shared memory, f32 accumulators in
-//               TMEM, 8 x K=16 per stage; tcgen05.commit releases the stages.
-//               For narrow token tiles the 8 MMAs of a stage rotate over up to
-//               four accumulators, so consecutive MMAs do not wait on each
-//               other's results; the epilogue adds the chains.
-//   warps 2..9  dequantizers, then the epilogue.  They form two groups of four
+//   warps 1-2   MMA issuers: one thread each issues tcgen05.mma kind::f16 with A
+//               read from tensor memory and B from shared memory, f32
+//               accumulators in TMEM, 8 x K=16 per 128-K sub-stage;
+//               tcgen05.commit releases the stages.  With two issuers they take
+//               alternate sub-stages into separate accumulators.  For narrow
+//               token tiles the 8 MMAs of a sub-stage rotate over up to four
+//               accumulators, so consecutive MMAs do not wait on each other's
+//               results; the epilogue adds everything up.
+//   warps 3-10 dequantizers, then the epilogue.  They form two groups of four
 //               warps (one warp per TMEM lane quarter); the groups take
 //               alternate stages, so two stages are dequantized at once.  Each
 //               thread owns one weight row of its stage: it reads the codes from
@@ -50,7 +52,7 @@ namespace tc {
 constexpr int kGroups = 2;      // dequant warp groups working on different sub-stages
 constexpr int kDqWarps = 4 * kGroups;
 constexpr int kDqThreads = kDqWarps * 32;
-constexpr int kMmaWarps = 1;    // MMA issuing warps
+constexpr int kMmaWarps = 2;    // MMA issuing warps (the plan may use one)
 constexpr int kDqWarp0 = 1 + kMmaWarps;
 constexpr int kThreads = 32 * (kDqWarp0 + kDqWarps);
 constexpr int kTileN = 128;     // weight rows per tile = MMA M
@@ -229,14 +231,20 @@ __device__ __forceinline__ void tmem_st_wait() {
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), version 1 for sm_100.
+// The low word holds the start address (16-byte units, bits 0-13) and LBO
+// (unused for swizzled K-major); adding a byte offset >> 4 to it moves the
+// start address as long as the result stays inside shared memory.
+__device__ __forceinline__ uint32_t sw128_desc_lo(uint32_t saddr) {
+  return ((saddr & 0x3FFFFu) >> 4) | (1u << 16);
+}
+__device__ __forceinline__ uint64_t sw128_desc_from(uint32_t lo) {
+  constexpr uint32_t hi = (1024u >> 4)     // SBO
+                          | (1u << 14)     // descriptor version (bit 46)
+                          | (2u << 29);    // SWIZZLE_128B (bits 61-63)
+  return ((uint64_t)hi << 32) | lo;
+}
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
-  d |= (uint64_t)1 << 46;                 // descriptor version
-  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
-  return d;
+  return sw128_desc_from(sw128_desc_lo(saddr));
 }
 
 // Instruction descriptor: kind::f16, f32 accumulator, f16 A and B, both
@@ -341,6 +349,54 @@ __device__ __forceinline__ void dequant_q4(const uint8_t* wst, int r, int q4, co
           o[2 * j + q] = h2_bits(v);
         }
       }
+    }
+  }
+}
+
+// A whole 128-K row of a sub-stage -> 64 f16x2 words in K order.  All of the
+// row's code vectors are loaded before any arithmetic so the loads overlap.
+// Group-128 int4: the pair (k0+2i, k0+2i+1) of a code word sits in nibbles
+// (i, i+4); nibbles 0/4 and 1/5 are masked in place (1024 + q and 1024 + 16q
+// as f16), nibbles 2/6 and 3/7 after one shift by 8.  (1024 + q) - (1024 + z)
+// and (1024 + 16q) / 16 - (64 + z) are both exact, so every word equals the
+// per-pair form: (q - z) exactly, then one rounding for * s.
+template <int FMT>
+__device__ __forceinline__ void dequant_row(const uint8_t* wst, int r, const uint8_t* tst,
+                                            int t_rows, int axis, int64_t n_row, int j_sub,
+                                            int sub, uint32_t (&o)[64]) {
+  if constexpr (FMT == F_INT4G) {
+    uint32_t w[16];
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      const uint4 c = *reinterpret_cast<const uint4*>(wst + r * 64 + ((q4 ^ ((r >> 1) & 3)) << 4));
+      w[4 * q4] = c.x;
+      w[4 * q4 + 1] = c.y;
+      w[4 * q4 + 2] = c.z;
+      w[4 * q4 + 3] = c.w;
+    }
+    const __half s = reinterpret_cast<const __half*>(tst)[j_sub * kTileN + r];
+    const __half z = reinterpret_cast<const __half*>(tst)[(sub + j_sub) * kTileN + r];
+    const __half2 off1 = __half2half2(__hadd(z, __float2half_rn(1024.0f)));
+    const __half2 neg_off16 = __half2half2(__hneg(__hadd(z, __float2half_rn(64.0f))));
+    const __half2 sixteenth = __float2half2_rn(0.0625f);
+    const __half2 sc = __half2half2(s);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t lo = w[i], hi = w[i] >> 8;
+      const __half2 t0 = bits_h2((lo & 0x000F000Fu) | 0x64006400u);
+      const __half2 t1 = bits_h2((lo & 0x00F000F0u) | 0x64006400u);
+      const __half2 t2 = bits_h2((hi & 0x000F000Fu) | 0x64006400u);
+      const __half2 t3 = bits_h2((hi & 0x00F000F0u) | 0x64006400u);
+      o[4 * i] = h2_bits(__hmul2(__hsub2(t0, off1), sc));
+      o[4 * i + 1] = h2_bits(__hmul2(__hfma2(t1, sixteenth, neg_off16), sc));
+      o[4 * i + 2] = h2_bits(__hmul2(__hsub2(t2, off1), sc));
+      o[4 * i + 3] = h2_bits(__hmul2(__hfma2(t3, sixteenth, neg_off16), sc));
+    }
+  } else {
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      uint32_t (&part)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[16 * q4]);
+      dequant_q4<FMT>(wst, r, q4, tst, t_rows, axis, n_row, j_sub, sub, part);
     }
   }
 }
@@ -521,9 +577,25 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     // issuer i takes the unit's sub-stages with local index % issuers == i
     const int issuer = warp - 1;
     if (lane == 0 && issuer < p.issuers) {
+      // The issuing thread shares its scheduler with two dequant warps, so the
+      // per-MMA work is kept to an add and the MMA itself: B descriptor offsets
+      // (16-byte units) and accumulator columns of the 8 MMAs of a sub-stage
+      // are fixed for the launch, ring slots advance by increment.
       const uint32_t idesc = make_idesc(p.bn);
       const uint32_t acc0 = tmem + (uint32_t)(issuer * p.chains * p.acc_cols);
-      int ti = 0, si = 0, unit_i = 0;
+      uint32_t boff[kBK / 16], dcol[kBK / 16];
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        boff[kk] = (uint32_t)(((kk >> 2) * p.bn * 128 + (kk & 3) * 32) >> 4);
+        dcol[kk] = acc0 + (uint32_t)((kk & (p.chains - 1)) * p.acc_cols);
+      }
+      // MMAs kk < chains of a unit's first sub-stage start their chain (no accumulate)
+      const uint32_t fresh_mask = 0xFFu & ~((1u << p.chains) - 1u);
+      const uint32_t x_lo0 = sw128_desc_lo(smem_u32(x_ring));
+      const uint32_t x_stage16 = (uint32_t)x_stage_bytes >> 4, x_sub16 = (uint32_t)x_sub_bytes >> 4;
+      uint32_t s = 0, s_ph = 0;   // TMA ring slot and its phase parity
+      uint32_t a = 0, a_ph = 0;   // A ring slot and its phase parity
+      int unit_i = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
         int nt, mt, ks0, ks1, sp;
@@ -533,40 +605,45 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           break;
         }
         tc_fence_after();
-        bool fresh = true;
-        for (int ks = ks0; ks < ks1 && ok; ks += sub, ++ti) {
-          const int s = ti % ns;
+        uint32_t mask = fresh_mask;
+        int lsub = 0;   // sub-stage index within the unit
+        for (int ks = ks0; ks < ks1 && ok; ks += sub) {
           const int nsub = min(sub, ks1 - ks);
-          const uint32_t x_stage = smem_u32(x_ring + s * x_stage_bytes);
+          const uint32_t x_lo = x_lo0 + s * x_stage16;
           // Every role that arrives on empty[s] first waits for this use of the
           // stage to land, so no arrival can be credited to an earlier phase.
-          if (!mbar_wait(&full[s], (ti / ns) & 1, abort_flag)) {
+          if (!mbar_wait(&full[s], s_ph, abort_flag)) {
             ok = false;
             break;
           }
-          for (int j = 0; j < nsub; ++j, ++si) {
-            if ((ks - ks0 + j) % p.issuers != issuer) continue;
-            const int a = si % na;
-            // afull implies the stage's TMA landed: the dequant warps waited on it
-            if (!mbar_wait(&afull[a], (si / na) & 1, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t a_col = tmem_a + (uint32_t)(a * kACols);
-            const uint32_t x_base = x_stage + (uint32_t)(j * x_sub_bytes);
-            const int chains = p.chains;
+          for (int j = 0; j < nsub; ++j, ++lsub) {
+            if (p.issuers == 1 || (lsub & 1) == issuer) {
+              // afull implies the stage's TMA landed: the dequant warps waited on it
+              if (!mbar_wait(&afull[a], a_ph, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t a_col = tmem_a + a * (uint32_t)kACols;
+              const uint32_t xb = x_lo + (uint32_t)j * x_sub16;
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t bd = sw128_desc(x_base + (kk >> 2) * (p.bn * 128) + (kk & 3) * 32);
-              const int c = kk & (chains - 1);
-              tc_mma_ts(acc0 + (uint32_t)(c * p.acc_cols), a_col + (uint32_t)(kk * 8), bd, idesc,
-                        (!fresh || kk >= chains) ? 1u : 0u);
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                tc_mma_ts(dcol[kk], a_col + (uint32_t)(kk * 8), sw128_desc_from(xb + boff[kk]),
+                          idesc, (mask >> kk) & 1u);
+              mask = 0xFFu;
+              tc_commit(&aempty[a]);
             }
-            fresh = false;
-            tc_commit(&aempty[a]);
+            if (++a == (uint32_t)na) {
+              a = 0;
+              a_ph ^= 1u;
+            }
           }
-          if (ok) tc_commit(&empty[s]);
+          if (!ok) break;
+          tc_commit(&empty[s]);
+          if (++s == (uint32_t)ns) {
+            s = 0;
+            s_ph ^= 1u;
+          }
         }
         if (!ok) break;
         tc_commit(accfull);
@@ -584,52 +661,58 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     const int gt = dt & 127;                      // thread index within the group
     const int row = quarter * 32 + lane;          // weight row = accumulator lane
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    int ti = 0, si = 0, unit_i = 0;
+    uint32_t s = 0, s_ph = 0;   // TMA ring slot and its phase parity
+    uint32_t a = 0, a_ph = 0;   // A ring slot and its phase parity
+    int unit_i = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
       const int64_t n = (int64_t)nt * kTileN + row;
-      for (int ks = ks0; ks < ks1 && ok; ks += sub, ++ti) {
-        const int s = ti % ns;
+      int lsub = 0;   // sub-stage index within the unit; group lsub % kGroups takes it
+      for (int ks = ks0; ks < ks1 && ok; ks += sub) {
         const int nsub = min(sub, ks1 - ks);
         // wait for this use of the stage even without a sub-stage to dequantize:
         // the arrival on empty[s] below must not run ahead of the producer
-        if (!mbar_wait(&full[s], (ti / ns) & 1, abort_flag)) {
+        if (!mbar_wait(&full[s], s_ph, abort_flag)) {
           ok = false;
           break;
         }
-        for (int j = 0; j < nsub; ++j, ++si) {
-          if ((ks - ks0 + j) % kGroups != group) continue;   // another group takes it
-          const int a = si % na;
-          if (!mbar_wait(&aempty[a], ((si / na) & 1) ^ 1, abort_flag)) {
-            ok = false;
-            break;
+        for (int j = 0; j < nsub; ++j, ++lsub) {
+          if (lsub % kGroups == group) {
+            if (!mbar_wait(&aempty[a], a_ph ^ 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint8_t* wst = w_ring + s * p.w_stage_bytes + j * w_sub_bytes;
+            const uint8_t* tst = t_ring + s * p.t_stage_bytes;
+            uint32_t o[64];
+            dequant_row<FMT>(wst, row, tst, p.t_rows, p.axis, n, j, sub, o);
+            const uint32_t a_addr = tmem_a + lane_addr + a * (uint32_t)kACols;
+            tmem_st32(a_addr, *reinterpret_cast<const uint32_t(*)[32]>(&o[0]));
+            tmem_st32(a_addr + 32u, *reinterpret_cast<const uint32_t(*)[32]>(&o[32]));
+            if (p.x_bf16) {
+              uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
+              for (int i = gt; i < x_sub_bytes / 16; i += 128) bf16_to_f16_chunk(xs + i);
+              fence_proxy_async();
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&afull[a]);
           }
-          const uint8_t* wst = w_ring + s * p.w_stage_bytes + j * w_sub_bytes;
-          const uint8_t* tst = t_ring + s * p.t_stage_bytes;
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            uint32_t o[32];
-            uint32_t (&lo)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[0]);
-            uint32_t (&hi)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[16]);
-            dequant_q4<FMT>(wst, row, 2 * h, tst, p.t_rows, p.axis, n, j, sub, lo);
-            dequant_q4<FMT>(wst, row, 2 * h + 1, tst, p.t_rows, p.axis, n, j, sub, hi);
-            tmem_st32(tmem_a + lane_addr + (uint32_t)(a * kACols + h * 32), o);
+          if (++a == (uint32_t)na) {
+            a = 0;
+            a_ph ^= 1u;
           }
-          if (p.x_bf16) {
-            uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
-            for (int i = gt; i < x_sub_bytes / 16; i += 128) bf16_to_f16_chunk(xs + i);
-            fence_proxy_async();
-          }
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[a]);
         }
         if (!ok) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);   // this warp is done with the stage
+        if (++s == (uint32_t)ns) {
+          s = 0;
+          s_ph ^= 1u;
+        }
       }
       if (!ok) break;
 
@@ -687,16 +770,28 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         finalize_here = *s_ticket != 0;
         if (finalize_here) {
           __threadfence();
-          for (int j = 0; j < p.bn; ++j) {
-            if (((j >> 3) % kGroups) != group) continue;   // same column ownership as above
-            const int64_t m = m0 + j;
-            float acc = 0.0f;
-            if (m < p.M && n < p.N) {
-              acc = __ldcg(p.ws + m * p.N + n);
-              for (int q = 1; q < p.splits; ++q)
-                acc += __ldcg(p.ws + ((int64_t)q * p.M + m) * p.N + n);
+          // same column ownership as above; the 8 tokens of a chunk load together
+          // (one L2 round trip per split), and splits add in split order
+          for (int c0 = 8 * group; c0 < p.bn; c0 += 8 * kGroups) {
+            float acc[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int64_t m = m0 + c0 + jj;
+              acc[jj] = (m < p.M && n < p.N) ? __ldcg(p.ws + m * p.N + n) : 0.0f;
             }
-            epi.emit(m, n, acc * nscale, lane);
+            for (int q = 1; q < p.splits; ++q) {
+              const float* part = p.ws + (int64_t)q * p.M * p.N;
+              float v[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                const int64_t m = m0 + c0 + jj;
+                v[jj] = (m < p.M && n < p.N) ? __ldcg(part + m * p.N + n) : 0.0f;
+              }
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) acc[jj] += v[jj];
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) epi.emit(m0 + c0 + jj, n, acc[jj] * nscale, lane);
           }
           if (dt == 0) p.counters[tile_id] = 0u;
         }
@@ -804,9 +899,10 @@ int fmt_of(const ie_qweight& w) {
   return w.axis == IE_AXIS_GROUP128 ? F_INT4G : F_INT4SYM;
 }
 
-// Tile/split choice: BN covers the tokens (<= 256 per tile); splits of K raise
-// the unit count toward a whole number of waves over the SMs, discounted by the
-// extra f32 partial traffic they cost relative to the weight bytes.
+// Tile/split choice: BN covers the tokens (<= 256 per tile).  The split count
+// minimises the slowest CTA's time in TMA-stage units: the stages of its units,
+// a fixed cost per unit (pipeline drain and epilogue) and per split-K finalize,
+// plus the f32 partials' extra traffic spread over the SMs.
 Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   Plan pl;
   pl.fmt = fmt_of(a.w);
@@ -823,8 +919,8 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
     pl.sub /= 2;
   pl.w_stage_bytes = row_stage * kTileN * pl.sub;
   const int sms = sm_count();
-  const double wbytes = (double)a.w.n * a.w.k * (row_stage / (double)kBK);
-  double best = -1.0;
+  constexpr double kUnitCost = 1.5, kFinalizeCost = 1.5;
+  double best = 1e300;
   const int tiles = pl.n_tiles * pl.m_tiles;
   const int tst = (pl.kstages + pl.sub - 1) / pl.sub;   // TMA stages along K
   for (int s = 1; s <= (allow_split ? 16 : 1); ++s) {
@@ -834,11 +930,11 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
     if ((s - 1) * per >= tst) continue;
     const int units = tiles * s;
     const int waves = (units + sms - 1) / sms;
-    const double eff = (double)units / ((double)waves * sms);
-    const double extra = s > 1 ? (2.0 * s * (double)M * a.w.n * 4.0) / wbytes : 0.0;
-    const double score = eff / (1.0 + extra);
-    if (score > best + 1e-9) {
-      best = score;
+    const double partial =
+        s > 1 ? 2.0 * s * (double)M * a.w.n * 4.0 / ((double)sms * pl.w_stage_bytes) : 0.0;
+    const double t = waves * (per + kUnitCost + (s > 1 ? kFinalizeCost : 0.0)) + partial;
+    if (t < best - 1e-9) {
+      best = t;
       pl.splits = s;
     }
   }
@@ -850,13 +946,15 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
     pl.t_rows = a.w.gate_up ? 2 : 1;
     pl.t_stage_bytes = ((pl.t_rows * kBK * 4 * pl.sub + 1023) / 1024) * 1024;
   }
-  // TMEM: accumulator columns (power of two >= 32) then the A ring, 64 columns a stage
-  // narrow tiles rotate their MMAs over independent accumulator chains and two
-  // issuing threads (one tcgen05.mma M=128 K=16 costs ~50 cycles to issue, and
-  // two issuers overlap)
+  // TMEM: accumulators, then the A ring (64 columns a sub-stage).  Narrow token
+  // tiles rotate their MMAs over independent accumulator chains, and two issuing
+  // threads take alternate sub-stages into separate accumulators whenever TMEM
+  // holds both sets next to a 4-deep A ring: a single issuer leaves the tensor
+  // pipe idle between its sub-stages (barrier wait, fence, commit), and shares
+  // its scheduler with two dequant warps.
   pl.acc_cols = ((pl.bn + 15) / 16) * 16;
-  pl.issuers = 1;
   pl.chains = pl.bn <= 32 ? 4 : (pl.bn <= 64 ? 2 : 1);
+  pl.issuers = (2 * pl.acc_cols * pl.chains + kMaxAStages * kACols <= 512) ? 2 : 1;
   const int accs = pl.acc_cols * pl.chains * pl.issuers;
   pl.na = (accs + kMaxAStages * kACols <= 512) ? kMaxAStages : 2;
   pl.tmem_cols = 32;
