@@ -58,7 +58,7 @@ constexpr int kThreads = 32 * (kDqWarp0 + kDqWarps);
 constexpr int kTileN = 128;     // weight rows per tile = MMA M
 constexpr int kBK = 128;        // K per stage (one int4 group)
 constexpr int kACols = kBK / 2; // TMEM columns of one A stage (two f16 per column)
-constexpr int kMaxAStages = 4;
+constexpr int kMaxAStages = 6;
 constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 2 GHz
 constexpr int kMinSmem = 120 * 1024;              // keeps one CTA per SM
 
@@ -167,9 +167,6 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void named_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -191,14 +188,17 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The loaded registers are defined only once tcgen05.wait::ld returns, so the
+// load and the wait form one asm statement (no use can be scheduled between).
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
@@ -479,7 +479,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint64_t* accfull = aempty + na;       // every issuer's MMAs of a unit done -> epilogue
   uint64_t* accempty = accfull + 1;      // epilogue -> MMA (count 1)
   uint64_t* mma_done = accempty + 1;     // [kMmaWarps] final commits: all MMAs retired
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + kMmaWarps);
+  uint64_t* dqbar = mma_done + kMmaWarps;   // bounded barrier of the dequant threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dqbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(abort_flag) + 1;
 
@@ -498,6 +499,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     mbar_init(accfull, p.issuers);
     mbar_init(accempty, 1);
     for (int i = 0; i < kMmaWarps; ++i) mbar_init(&mma_done[i], 1);
+    mbar_init(dqbar, kDqThreads);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -665,6 +667,16 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     uint32_t a = 0, a_ph = 0;   // A ring slot and its phase parity
     int unit_i = 0;
     bool ok = true;
+    // Barrier of the dequant threads with a bounded wait (bar.sync cannot give
+    // up): if one warp leaves on an expired wait, the others follow it out
+    // instead of blocking the CTA's teardown.
+    uint32_t dq_ph = 0;
+    auto dq_sync = [&]() -> bool {
+      mbar_arrive(dqbar);
+      const bool done = mbar_wait(dqbar, dq_ph, abort_flag);
+      dq_ph ^= 1u;
+      return done;
+    };
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
@@ -753,7 +765,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
       tc_fence_before();
-      named_sync(1, kDqThreads);
+      if (!dq_sync()) {
+        ok = false;
+        break;
+      }
       if (dt == 0) mbar_arrive(accempty);
 
       const int tile_id = mt * p.n_tiles + nt;
@@ -761,12 +776,18 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (split) {
         // ticket: the last split to arrive sums all splits in split order
         __threadfence();
-        named_sync(1, kDqThreads);
+        if (!dq_sync()) {
+          ok = false;
+          break;
+        }
         if (dt == 0) {
           const uint32_t t = atomicAdd(&p.counters[tile_id], 1u);
           *s_ticket = (t == (uint32_t)(p.splits - 1)) ? 1 : 0;
         }
-        named_sync(1, kDqThreads);
+        if (!dq_sync()) {
+          ok = false;
+          break;
+        }
         finalize_here = *s_ticket != 0;
         if (finalize_here) {
           __threadfence();
@@ -797,7 +818,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
       if (reduce && finalize_here) {
-        named_sync(1, kDqThreads);
+        if (!dq_sync()) {
+          ok = false;
+          break;
+        }
         if (dt < rc.world) {
           __threadfence_system();
           st_release_sys(rc.flags[dt] + (int64_t)tile_id * kMaxWorld + rc.rank, epoch);
@@ -954,9 +978,12 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   // its scheduler with two dequant warps.
   pl.acc_cols = ((pl.bn + 15) / 16) * 16;
   pl.chains = pl.bn <= 32 ? 4 : (pl.bn <= 64 ? 2 : 1);
-  pl.issuers = (2 * pl.acc_cols * pl.chains + kMaxAStages * kACols <= 512) ? 2 : 1;
+  pl.issuers = (2 * pl.acc_cols * pl.chains + 4 * kACols <= 512) ? 2 : 1;
   const int accs = pl.acc_cols * pl.chains * pl.issuers;
-  pl.na = (accs + kMaxAStages * kACols <= 512) ? kMaxAStages : 2;
+  // The A ring covers a sub-stage's dequant plus its MMAs' latency (8 MMAs take
+  // ~0.45 us from issue to commit), so it is as deep as TMEM allows.
+  pl.na = accs + kMaxAStages * kACols <= 512 ? kMaxAStages
+                                             : (accs + 4 * kACols <= 512 ? 4 : 2);
   pl.tmem_cols = 32;
   while (pl.tmem_cols < accs + pl.na * kACols) pl.tmem_cols *= 2;
   const size_t x_stage = (size_t)pl.bn * kBK * 2 * pl.sub;
@@ -965,7 +992,7 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   const size_t per = x_stage + pl.w_stage_bytes + pl.t_stage_bytes;
   pl.ns = (int)std::min<size_t>(12, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
-  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps) + 16;
+  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 1) + 16;
   if (pl.smem < (size_t)kMinSmem) pl.smem = kMinSmem;   // one CTA per SM: TMEM and co-residency
   if (pl.splits > 1) {
     pl.counters_bytes = (((size_t)tiles * 4) + 255) / 256 * 256;
