@@ -182,6 +182,32 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+PROFILE = REPO / "profiles" / "qgemm_tc_int4g128_b16_ncu_full.md"
+
+
+def measured_traffic(args, kern_bytes: float, shape) -> tuple:
+    """DRAM bytes (read + write) of one gate/up launch, from the committed ncu
+    capture of the same kernel at TP=1, batch 16, int4-g128, scaled to this
+    rank's launch by its algorithmic bytes (the traffic grows with the weight
+    rows a rank owns).  None when the workload differs from the capture's."""
+    if args.scheme != "int4-g128" or args.batch != 16:
+        return None, "no capture for this scheme/batch"
+    try:
+        text = PROFILE.read_text()
+    except OSError:
+        return None, "profile summary missing"
+    for line in text.splitlines():
+        if "traffic_bytes_per_launch:" in line:
+            field = line.split("traffic_bytes_per_launch:")[1].split()[0]
+            measured = float(field.strip("`.,"))
+            break
+    else:
+        return None, "profile summary has no traffic line"
+    h, i = shape.hidden, shape.intermediate
+    tp1 = (h * 2 * i / 2 + (h // 128) * 2 * i * 4) + args.batch * h * 2 + args.batch * i * 2
+    return measured * kern_bytes / tp1, f"ncu dram__bytes_read+write, {PROFILE.name}"
+
+
 def workload_config(args, world: int) -> dict:
     return {"workload": (f"Llama-3-8B-shaped decoder, quantized linear path of one decode step "
                          f"({args.layers} layers: qkv, o+allreduce, gate/up+SiLU, "
@@ -302,6 +328,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     inter = 2 * shape.intermediate // world
     kern_bytes = wb["gate_up"] + args.batch * shape.hidden * 2 + args.batch * (inter // 2) * 2
     achieved = kern_bytes / (kern_ms / 1e3) / 1e9
+    traffic, traffic_src = measured_traffic(args, kern_bytes, shape)
     peaks = {}
     try:
         peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
@@ -317,7 +344,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": traffic,
+                         "traffic_source": traffic_src,
                          "kernel": ("qgemm_tc_kernel (tcgen05) gate/up, int4-g128, fused SiLU*up"
                                     if args.batch >= 2 else
                                     "gemv_kernel gate/up, int4-g128, fused SiLU*up"),
