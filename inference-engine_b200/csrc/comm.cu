@@ -84,10 +84,10 @@ allreduce_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t n, Reduc
         landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + e] = v;
     }
     __syncthreads();
-    if (threadIdx.x < rc.world) {
-      __threadfence_system();
+    // st.release.sys publishes the block's pushes: bar.sync orders them before
+    // this thread's release, and a peer's ld.acquire.sys of the flag then sees them
+    if (threadIdx.x < rc.world)
       st_release_sys(rc.flags[threadIdx.x] + t * kMaxWorld + rc.rank, epoch);
-    }
   }
   __shared__ int s_ok;
   const float* mine = landing_slot(rc, rc.rank, epoch);

@@ -329,10 +329,10 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
         landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + gm * p.N + n] = tile[e];
     }
     __syncthreads();
-    if (threadIdx.x < rc.world) {
-      __threadfence_system();
+    // st.release.sys publishes the block's pushes: bar.sync orders them before
+    // this thread's release, and a peer's ld.acquire.sys of the flag then sees them
+    if (threadIdx.x < rc.world)
       st_release_sys(rc.flags[threadIdx.x] + t * kMaxWorld + rc.rank, epoch);
-    }
   }
 
   if (!reduce) return;

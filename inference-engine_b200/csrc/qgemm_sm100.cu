@@ -822,10 +822,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           ok = false;
           break;
         }
-        if (dt < rc.world) {
-          __threadfence_system();
+        // st.release.sys publishes every dequant thread's pushes: the mbarrier
+        // above (release/acquire at CTA scope) orders them before this release,
+        // and a peer's ld.acquire.sys of the flag then sees them
+        if (dt < rc.world)
           st_release_sys(rc.flags[dt] + (int64_t)tile_id * kMaxWorld + rc.rank, epoch);
-        }
       }
     }
     if (!ok) *abort_flag = 1;
@@ -856,16 +857,46 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       __syncthreads();
       if (!s_ok) break;
       const int nt = t % p.n_tiles, mt = t / p.n_tiles;
-      for (int e = threadIdx.x; e < kTileN * p.bn; e += kThreads) {
-        const int64_t n = (int64_t)nt * kTileN + (e % kTileN);
-        const int64_t m = (int64_t)mt * p.bn + (e / kTileN);
-        if (m >= p.M || n >= p.N) continue;
-        const int64_t off = m * p.N + n;
-        float v = mine[off];
-        for (int src = 1; src < rc.world; ++src) v += mine[src * rc.slot_floats + off];
-        if (p.epilogue & IE_EPI_BIAS) v += p.bias[n];
-        if (p.epilogue & IE_EPI_RESIDUAL) v = load_val(p.residual, p.out_dtype, m * p.ldr + n) + v;
-        store_val(p.out, p.out_dtype, m * p.ldo + n, v);
+      // kPer elements per thread and round, all of whose loads (every rank's
+      // slot, the residual) are in flight together: one L2 round trip per round
+      // instead of one per element; ranks still add in rank order
+      constexpr int kPer = 8;
+      for (int e0 = threadIdx.x; e0 < kTileN * p.bn; e0 += kThreads * kPer) {
+        int64_t off[kPer], n[kPer], m[kPer];
+        bool valid[kPer];
+        float v[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int e = e0 + j * kThreads;
+          n[j] = (int64_t)nt * kTileN + (e % kTileN);
+          m[j] = (int64_t)mt * p.bn + (e / kTileN);
+          valid[j] = e < kTileN * p.bn && m[j] < p.M && n[j] < p.N;
+          off[j] = valid[j] ? m[j] * p.N + n[j] : 0;
+          v[j] = valid[j] ? __ldcg(mine + off[j]) : 0.0f;
+        }
+        for (int src = 1; src < rc.world; ++src) {
+          const float* slot = mine + (int64_t)src * rc.slot_floats;
+          float w[kPer];
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) w[j] = valid[j] ? __ldcg(slot + off[j]) : 0.0f;
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) v[j] += w[j];
+        }
+        if (p.epilogue & IE_EPI_BIAS) {
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) v[j] += valid[j] ? p.bias[n[j]] : 0.0f;
+        }
+        if (p.epilogue & IE_EPI_RESIDUAL) {
+          float r[kPer];
+#pragma unroll
+          for (int j = 0; j < kPer; ++j)
+            r[j] = valid[j] ? load_val(p.residual, p.out_dtype, m[j] * p.ldr + n[j]) : 0.0f;
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) v[j] = r[j] + v[j];
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+          if (valid[j]) store_val(p.out, p.out_dtype, m[j] * p.ldo + n[j], v[j]);
       }
       __syncthreads();
     }
