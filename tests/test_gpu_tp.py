@@ -36,6 +36,27 @@ def test_rms_norm_matches_the_reference():
     np.testing.assert_allclose(got, o.rms_norm(x, w), rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("h", [4096, 8192, 1000, 13])
+def test_rms_norm_vector_and_scalar_rows(h):
+    """Hidden sizes that are multiples of 8 take the vector kernel (several
+    chunks per thread at 8192); 1000 is one too (125 chunks); 13 takes the
+    scalar loop.  bf16 in and out, compared with the f32 reference on the
+    same rounded inputs; strided rows take the scalar loop as well."""
+    x = o.seeded_activations(16, h, seed=h)
+    w = np.linspace(0.5, 1.5, h).astype(np.float32)
+    xb = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    want = o.rms_norm(xb.float().cpu().numpy(), w)
+    got = rms_norm(xb, w).float().cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=8e-3, atol=1e-5)   # one bf16 rounding
+    wide = torch.zeros((16, h + 3), dtype=torch.bfloat16, device="cuda")
+    wide[:, :h] = xb
+    got = rms_norm(wide[:, :h], w).float().cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=8e-3, atol=1e-5)
+    xf = torch.from_numpy(x).cuda()
+    np.testing.assert_allclose(rms_norm(xf, w).cpu().numpy(), o.rms_norm(x, w),
+                               rtol=1e-6, atol=1e-6)
+
+
 @pytest.mark.parametrize("world", [1, 2, 4])
 def test_sharded_mlp_matches_the_golden_tp_output(golden, world):
     x = golden["mlp_x"]
