@@ -49,7 +49,12 @@
 namespace ie {
 namespace tc {
 
-constexpr int kGroups = 2;      // dequant warp groups working on different sub-stages
+// Dequant warps: groups of four (one per TMEM lane quarter).  kPairs sub-stages
+// are in flight at once, each split between kHalves groups by K (64 K apiece),
+// so more, shorter dependency chains hide the ALU and TMEM-store latencies.
+constexpr int kPairs = 2;
+constexpr int kHalves = 2;
+constexpr int kGroups = kPairs * kHalves;
 constexpr int kDqWarps = 4 * kGroups;
 constexpr int kDqThreads = kDqWarps * 32;
 constexpr int kMmaWarps = 2;    // MMA issuing warps (the plan may use one)
@@ -353,26 +358,29 @@ __device__ __forceinline__ void dequant_q4(const uint8_t* wst, int r, int q4, co
   }
 }
 
-// A whole 128-K row of a sub-stage -> 64 f16x2 words in K order.  All of the
-// row's code vectors are loaded before any arithmetic so the loads overlap.
+// One 64-K half (`half` 0 or 1) of a 128-K row of a sub-stage -> 32 f16x2
+// words in K order.  The half's code vectors are loaded before any arithmetic
+// so the loads overlap.
 // Group-128 int4: the pair (k0+2i, k0+2i+1) of a code word sits in nibbles
 // (i, i+4); nibbles 0/4 and 1/5 are masked in place (1024 + q and 1024 + 16q
 // as f16), nibbles 2/6 and 3/7 after one shift by 8.  (1024 + q) - (1024 + z)
 // and (1024 + 16q) / 16 - (64 + z) are both exact, so every word equals the
 // per-pair form: (q - z) exactly, then one rounding for * s.
 template <int FMT>
-__device__ __forceinline__ void dequant_row(const uint8_t* wst, int r, const uint8_t* tst,
-                                            int t_rows, int axis, int64_t n_row, int j_sub,
-                                            int sub, uint32_t (&o)[64]) {
+__device__ __forceinline__ void dequant_half(const uint8_t* wst, int r, int half,
+                                             const uint8_t* tst, int t_rows, int axis,
+                                             int64_t n_row, int j_sub, int sub,
+                                             uint32_t (&o)[32]) {
   if constexpr (FMT == F_INT4G) {
-    uint32_t w[16];
+    uint32_t w[8];
 #pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int q4 = 2 * half + c2;
       const uint4 c = *reinterpret_cast<const uint4*>(wst + r * 64 + ((q4 ^ ((r >> 1) & 3)) << 4));
-      w[4 * q4] = c.x;
-      w[4 * q4 + 1] = c.y;
-      w[4 * q4 + 2] = c.z;
-      w[4 * q4 + 3] = c.w;
+      w[4 * c2] = c.x;
+      w[4 * c2 + 1] = c.y;
+      w[4 * c2 + 2] = c.z;
+      w[4 * c2 + 3] = c.w;
     }
     const __half s = reinterpret_cast<const __half*>(tst)[j_sub * kTileN + r];
     const __half z = reinterpret_cast<const __half*>(tst)[(sub + j_sub) * kTileN + r];
@@ -381,7 +389,7 @@ __device__ __forceinline__ void dequant_row(const uint8_t* wst, int r, const uin
     const __half2 sixteenth = __float2half2_rn(0.0625f);
     const __half2 sc = __half2half2(s);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const uint32_t lo = w[i], hi = w[i] >> 8;
       const __half2 t0 = bits_h2((lo & 0x000F000Fu) | 0x64006400u);
       const __half2 t1 = bits_h2((lo & 0x00F000F0u) | 0x64006400u);
@@ -394,9 +402,9 @@ __device__ __forceinline__ void dequant_row(const uint8_t* wst, int r, const uin
     }
   } else {
 #pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      uint32_t (&part)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[16 * q4]);
-      dequant_q4<FMT>(wst, r, q4, tst, t_rows, axis, n_row, j_sub, sub, part);
+    for (int c2 = 0; c2 < 2; ++c2) {
+      uint32_t (&part)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[16 * c2]);
+      dequant_q4<FMT>(wst, r, 2 * half + c2, tst, t_rows, axis, n_row, j_sub, sub, part);
     }
   }
 }
@@ -474,7 +482,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + ns * p.t_stage_bytes);
   uint64_t* full = bars;                 // [ns]  TMA landed (count 1 + tx)
   uint64_t* empty = full + ns;           // [ns]  MMA done + every dequant warp done
-  uint64_t* afull = empty + ns;          // [na]  one group's four warps wrote A
+  uint64_t* afull = empty + ns;          // [na]  a pair's 4 * kHalves warps wrote A
   uint64_t* aempty = afull + na;         // [na]  MMA read A (commit)
   uint64_t* accfull = aempty + na;       // every issuer's MMAs of a unit done -> epilogue
   uint64_t* accempty = accfull + 1;      // epilogue -> MMA (count 1)
@@ -493,7 +501,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       mbar_init(&empty[s], p.issuers + kDqWarps);   // each issuer's commit + every dequant warp
     }
     for (int s = 0; s < na; ++s) {
-      mbar_init(&afull[s], 4);
+      mbar_init(&afull[s], 4 * kHalves);
       mbar_init(&aempty[s], 1);
     }
     mbar_init(accfull, p.issuers);
@@ -659,8 +667,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     // ---------------------- dequantize + epilogue ----------------------
     const int dt = threadIdx.x - 32 * kDqWarp0;   // 0 .. kDqThreads-1
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter ..
-    const int group = (warp - kDqWarp0) >> 2;     // which sub-stages this warp dequantizes
-    const int gt = dt & 127;                      // thread index within the group
+    const int group = (warp - kDqWarp0) >> 2;     // 0 .. kGroups-1
+    const int pair = group / kHalves;             // which sub-stages this warp dequantizes
+    const int half = group % kHalves;             // and which 64-K half of them
+    const int pt = half * 128 + (dt & 127);       // thread index within the pair
     const int row = quarter * 32 + lane;          // weight row = accumulator lane
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     uint32_t s = 0, s_ph = 0;   // TMA ring slot and its phase parity
@@ -681,7 +691,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
       const int64_t n = (int64_t)nt * kTileN + row;
-      int lsub = 0;   // sub-stage index within the unit; group lsub % kGroups takes it
+      int lsub = 0;   // sub-stage index within the unit; pair lsub % kPairs takes it
       for (int ks = ks0; ks < ks1 && ok; ks += sub) {
         const int nsub = min(sub, ks1 - ks);
         // wait for this use of the stage even without a sub-stage to dequantize:
@@ -691,21 +701,19 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           break;
         }
         for (int j = 0; j < nsub; ++j, ++lsub) {
-          if (lsub % kGroups == group) {
+          if (lsub % kPairs == pair) {
             if (!mbar_wait(&aempty[a], a_ph ^ 1u, abort_flag)) {
               ok = false;
               break;
             }
             const uint8_t* wst = w_ring + s * p.w_stage_bytes + j * w_sub_bytes;
             const uint8_t* tst = t_ring + s * p.t_stage_bytes;
-            uint32_t o[64];
-            dequant_row<FMT>(wst, row, tst, p.t_rows, p.axis, n, j, sub, o);
-            const uint32_t a_addr = tmem_a + lane_addr + a * (uint32_t)kACols;
-            tmem_st32(a_addr, *reinterpret_cast<const uint32_t(*)[32]>(&o[0]));
-            tmem_st32(a_addr + 32u, *reinterpret_cast<const uint32_t(*)[32]>(&o[32]));
+            uint32_t o[32];
+            dequant_half<FMT>(wst, row, half, tst, p.t_rows, p.axis, n, j, sub, o);
+            tmem_st32(tmem_a + lane_addr + a * (uint32_t)kACols + (uint32_t)(half * 32), o);
             if (p.x_bf16) {
               uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
-              for (int i = gt; i < x_sub_bytes / 16; i += 128) bf16_to_f16_chunk(xs + i);
+              for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) bf16_to_f16_chunk(xs + i);
               fence_proxy_async();
             }
             tmem_st_wait();
