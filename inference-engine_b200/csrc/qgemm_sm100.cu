@@ -436,25 +436,59 @@ struct Epi {
   const ReduceCtx& rc;
   uint32_t epoch;
   int reduce;
-  // Writes one finished row value; gate/up pairs combine lanes (n even, n+1).
-  __device__ __forceinline__ void emit(int64_t m, int64_t n, float val, int lane) const {
+  // Writes the finished values of the 8 tokens m0 .. m0+7 of row n; gate/up
+  // pairs combine lanes (n even, n+1).  Every shuffle, then every residual
+  // load, is issued before the stores, so the loads of one token do not wait
+  // behind the previous token's store (out may alias nothing, but the compiler
+  // cannot know).  SiLU divides with __fdividef (2 ulp), far below the
+  // bf16/f16 rounding of the output.
+  __device__ __forceinline__ void emit8(int64_t m0, int64_t n, float (&v)[8], int lane) const {
+    const bool has_res = (p.epilogue & IE_EPI_RESIDUAL) != 0;
     if (p.epilogue & IE_EPI_SILU_MUL) {
-      if (p.epilogue & IE_EPI_BIAS) val += (n < p.N) ? p.bias[n] : 0.0f;
-      const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
-      if ((lane & 1) == 0 && m < p.M && n + 1 < p.N) {
-        float o = (val / (1.0f + __expf(-val))) * partner;
-        const int64_t jcol = n >> 1;
-        if (p.epilogue & IE_EPI_RESIDUAL) o += load_val(p.residual, p.out_dtype, m * p.ldr + jcol);
-        store_val(p.out, p.out_dtype, m * p.ldo + jcol, o);
+      const float b = ((p.epilogue & IE_EPI_BIAS) && n < p.N) ? p.bias[n] : 0.0f;
+      float partner[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (p.epilogue & IE_EPI_BIAS) v[j] += b;
+        partner[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
       }
-    } else if (m < p.M && n < p.N) {
+      if ((lane & 1) == 0 && n + 1 < p.N) {
+        const int64_t jcol = n >> 1;
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          r[j] = (has_res && m0 + j < p.M) ? load_val(p.residual, p.out_dtype, (m0 + j) * p.ldr + jcol)
+                                           : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (m0 + j >= p.M) continue;
+          float o = __fdividef(v[j], 1.0f + __expf(-v[j])) * partner[j];
+          if (has_res) o += r[j];
+          store_val(p.out, p.out_dtype, (m0 + j) * p.ldo + jcol, o);
+        }
+      }
+    } else if (n < p.N) {
       if (reduce) {
-        for (int dst = 0; dst < rc.world; ++dst)
-          landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + m * p.N + n] = val;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (m0 + j < p.M)
+            for (int dst = 0; dst < rc.world; ++dst)
+              landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + (m0 + j) * p.N + n] = v[j];
       } else {
-        if (p.epilogue & IE_EPI_BIAS) val += p.bias[n];
-        if (p.epilogue & IE_EPI_RESIDUAL) val = load_val(p.residual, p.out_dtype, m * p.ldr + n) + val;
-        store_val(p.out, p.out_dtype, m * p.ldo + n, val);
+        const float b = (p.epilogue & IE_EPI_BIAS) ? p.bias[n] : 0.0f;
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          r[j] = (has_res && m0 + j < p.M) ? load_val(p.residual, p.out_dtype, (m0 + j) * p.ldr + n)
+                                           : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (m0 + j >= p.M) continue;
+          float val = v[j];
+          if (p.epilogue & IE_EPI_BIAS) val += b;
+          if (has_res) val = r[j] + val;
+          store_val(p.out, p.out_dtype, (m0 + j) * p.ldo + n, val);
+        }
       }
     }
   }
@@ -762,14 +796,16 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[j] += w[j];
         }
+        if (split) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int64_t m = m0 + c0 + j;
-          if (split) {
+          for (int j = 0; j < 8; ++j) {
+            const int64_t m = m0 + c0 + j;
             if (m < p.M && n < p.N) p.ws[((int64_t)sp * p.M + m) * p.N + n] = v[j];
-          } else {
-            epi.emit(m, n, v[j] * nscale, lane);
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] *= nscale;
+          epi.emit8(m0 + c0, n, v, lane);
         }
       }
       tc_fence_before();
@@ -820,7 +856,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
               for (int jj = 0; jj < 8; ++jj) acc[jj] += v[jj];
             }
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) epi.emit(m0 + c0 + jj, n, acc[jj] * nscale, lane);
+            for (int jj = 0; jj < 8; ++jj) acc[jj] *= nscale;
+            epi.emit8(m0 + c0, n, acc, lane);
           }
           if (dt == 0) p.counters[tile_id] = 0u;
         }
