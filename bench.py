@@ -346,9 +346,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_source": traffic_src,
-                         "kernel": ("qgemm_tc_kernel (tcgen05) gate/up, int4-g128, fused SiLU*up"
-                                    if args.batch >= 2 else
-                                    "gemv_kernel gate/up, int4-g128, fused SiLU*up"),
+                         "kernel": "qgemm_tc_kernel (tcgen05) gate/up, int4-g128, fused SiLU*up",
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
                          "algorithmic_bytes_per_launch": kern_bytes,
                          "launch_us": kern_ms * 1e3},

@@ -121,14 +121,14 @@ __device__ __forceinline__ float* landing_slot(const ReduceCtx& rc, int dst, uin
   return rc.landing[dst] + (int64_t)(epoch & 1u) * rc.parity_stride;
 }
 // Called by every CTA once at the end (after its last __syncthreads): the last
-// CTA publishes the new epoch and resets the completion counter.
+// CTA publishes the new epoch and resets the completion counter.  No fence is
+// needed: every CTA read the epoch at its start, before it counted itself
+// here, and the next call reads it only after this kernel has completed.
 __device__ __forceinline__ void reduce_finish(const ReduceCtx& rc, uint32_t epoch) {
   if (threadIdx.x == 0) {
-    __threadfence();
     if (atomicAdd(rc.done, 1u) == gridDim.x - 1) {
       *(volatile uint32_t*)rc.epoch_dev = epoch;
       *(volatile uint32_t*)rc.done = 0u;
-      __threadfence();
     }
   }
 }

@@ -97,6 +97,9 @@ struct TcParams {
   int t_stage_bytes;        // table bytes per stage (1024-aligned slot)
   int t_joint;              // group scale and zero tables are one [2][G][N] array
   int sub;                  // 128-K sub-stages per TMA stage
+  int csplit;               // the splits of a tile form one cluster (rank = split)
+  int nclusters;            // clusters in the grid (csplit)
+  int recv_bytes;           // csplit: leader's receive buffer [splits-1][bn][128] f32
   float* ws;                // split-K partials [splits][M][N]
   uint32_t* counters;       // per (m_tile, n_tile) tickets, self-resetting
 };
@@ -144,6 +147,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
   }
 }
+// Bounded wait with cluster-scope acquire (for arrivals from other CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  const volatile int* abort_flag);
 // Unconditional bounded drain wait used at teardown.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
@@ -165,6 +171,73 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
+}
+// ---- thread-block cluster helpers (cluster split-K) ----
+// The K splits of a tile run as one cluster: the non-leader CTAs store their
+// f32 partial tiles into the leader's shared memory (distributed shared memory)
+// and arrive on the leader's mbarrier; no global memory is involved.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `local` (a shared::cta address) in CTA `rank`
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// arrive on an mbarrier of another CTA of the cluster, releasing this thread's
+// prior writes at cluster scope
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+// try_wait with acquire at cluster scope (pairs with remote releases)
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Hardware barrier across the cluster's threads: used once after barrier
+// initialisation and once at teardown, points every CTA reaches on every path.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  const volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_tc_status, kErrWait);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// Ticket of a split-K tile: acquire-release at GPU scope, so the arriving CTA's
+// partials (ordered before this by a CTA barrier) are published with it and
+// the last CTA sees every earlier CTA's partials.
+__device__ __forceinline__ uint32_t ticket_add(uint32_t* p) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+  return old;
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -420,6 +493,44 @@ __device__ __forceinline__ float load_val(const void* in, int dt, int64_t i) {
   return static_cast<const float*>(in)[i];
 }
 
+// 8 values at base + j * stride (j < valid) of an activation-typed array; the
+// dtype is decided once for the 8, so the executed code is one straight run.
+__device__ __forceinline__ void load8(const void* in, int dt, int64_t base, int64_t stride,
+                                      int valid, float (&r)[8]) {
+  if (dt == IE_DT_BF16) {
+    const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(in) + base;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = j < valid ? __bfloat162float(q[j * stride]) : 0.0f;
+  } else if (dt == IE_DT_F16) {
+    const __half* q = static_cast<const __half*>(in) + base;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = j < valid ? __half2float(q[j * stride]) : 0.0f;
+  } else {
+    const float* q = static_cast<const float*>(in) + base;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = j < valid ? q[j * stride] : 0.0f;
+  }
+}
+__device__ __forceinline__ void store8(void* out, int dt, int64_t base, int64_t stride,
+                                       int valid, const float (&v)[8]) {
+  if (dt == IE_DT_BF16) {
+    __nv_bfloat16* q = static_cast<__nv_bfloat16*>(out) + base;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < valid) q[j * stride] = __float2bfloat16_rn(v[j]);
+  } else if (dt == IE_DT_F16) {
+    __half* q = static_cast<__half*>(out) + base;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < valid) q[j * stride] = __float2half_rn(v[j]);
+  } else {
+    float* q = static_cast<float*>(out) + base;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < valid) q[j * stride] = v[j];
+  }
+}
+
 // bf16 -> f16 of one 16-byte chunk (8 values), in place.
 __device__ __forceinline__ void bf16_to_f16_chunk(uint4* p) {
   uint4 v = *p;
@@ -442,8 +553,26 @@ struct Epi {
   // behind the previous token's store (out may alias nothing, but the compiler
   // cannot know).  SiLU divides with __fdividef (2 ulp), far below the
   // bf16/f16 rounding of the output.
-  __device__ __forceinline__ void emit8(int64_t m0, int64_t n, float (&v)[8], int lane) const {
+  // Residual values of those tokens (the half-width column for gate/up pairs),
+  // zero where there is none.
+  __device__ __forceinline__ void load_res8(int64_t m0, int64_t n, int lane, float (&r)[8]) const {
+    const bool silu = (p.epilogue & IE_EPI_SILU_MUL) != 0;
+    const bool want = (p.epilogue & IE_EPI_RESIDUAL) && !(reduce && !silu) &&
+                      (silu ? ((lane & 1) == 0 && n + 1 < p.N) : n < p.N);
+    const int64_t col = silu ? (n >> 1) : n;
+    const int valid = want ? (int)(p.M - m0 < 8 ? (int)(p.M - m0) : 8) : 0;
+    load8(p.residual, p.out_dtype, m0 * p.ldr + col, p.ldr, valid, r);
+  }
+  __device__ __forceinline__ void emit8(int64_t m0, int64_t n, float (&v)[8], int lane,
+                                        const float* pre_res = nullptr) const {
     const bool has_res = (p.epilogue & IE_EPI_RESIDUAL) != 0;
+    float r[8];
+    if (pre_res) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = pre_res[j];
+    } else {
+      load_res8(m0, n, lane, r);
+    }
     if (p.epilogue & IE_EPI_SILU_MUL) {
       const float b = ((p.epilogue & IE_EPI_BIAS) && n < p.N) ? p.bias[n] : 0.0f;
       float partner[8];
@@ -453,19 +582,13 @@ struct Epi {
         partner[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
       }
       if ((lane & 1) == 0 && n + 1 < p.N) {
-        const int64_t jcol = n >> 1;
-        float r[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          r[j] = (has_res && m0 + j < p.M) ? load_val(p.residual, p.out_dtype, (m0 + j) * p.ldr + jcol)
-                                           : 0.0f;
+        float o[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          if (m0 + j >= p.M) continue;
-          float o = __fdividef(v[j], 1.0f + __expf(-v[j])) * partner[j];
-          if (has_res) o += r[j];
-          store_val(p.out, p.out_dtype, (m0 + j) * p.ldo + jcol, o);
+          o[j] = __fdividef(v[j], 1.0f + __expf(-v[j])) * partner[j];
+          if (has_res) o[j] += r[j];
         }
+        store8(p.out, p.out_dtype, m0 * p.ldo + (n >> 1), p.ldo, (int)(p.M - m0 < 8 ? (int)(p.M - m0) : 8), o);
       }
     } else if (n < p.N) {
       if (reduce) {
@@ -476,19 +599,15 @@ struct Epi {
               landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + (m0 + j) * p.N + n] = v[j];
       } else {
         const float b = (p.epilogue & IE_EPI_BIAS) ? p.bias[n] : 0.0f;
-        float r[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          r[j] = (has_res && m0 + j < p.M) ? load_val(p.residual, p.out_dtype, (m0 + j) * p.ldr + n)
-                                           : 0.0f;
+        float o[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          if (m0 + j >= p.M) continue;
           float val = v[j];
           if (p.epilogue & IE_EPI_BIAS) val += b;
           if (has_res) val = r[j] + val;
-          store_val(p.out, p.out_dtype, (m0 + j) * p.ldo + n, val);
+          o[j] = val;
         }
+        store8(p.out, p.out_dtype, m0 * p.ldo + n, p.ldo, (int)(p.M - m0 < 8 ? (int)(p.M - m0) : 8), o);
       }
     }
   }
@@ -497,7 +616,10 @@ struct Epi {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int FMT>
+// CSPLIT: the K splits of a tile reduce inside a thread-block cluster instead
+// of through global partials; each instantiation carries only one of the two
+// paths, so neither takes registers from the dequant loop of the other.
+template <int FMT, bool CSPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                 const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
@@ -513,7 +635,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint8_t* x_ring = smem;                                   // ns x x_stage_bytes
   uint8_t* w_ring = x_ring + ns * x_stage_bytes;            // ns x w_stage_bytes
   uint8_t* t_ring = w_ring + ns * p.w_stage_bytes;          // ns x t_stage_bytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + ns * p.t_stage_bytes);
+  float* recv = reinterpret_cast<float*>(t_ring + ns * p.t_stage_bytes);   // csplit
+  uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + ns * p.t_stage_bytes + p.recv_bytes);
   uint64_t* full = bars;                 // [ns]  TMA landed (count 1 + tx)
   uint64_t* empty = full + ns;           // [ns]  MMA done + every dequant warp done
   uint64_t* afull = empty + ns;          // [na]  a pair's 4 * kHalves warps wrote A
@@ -522,7 +645,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint64_t* accempty = accfull + 1;      // epilogue -> MMA (count 1)
   uint64_t* mma_done = accempty + 1;     // [kMmaWarps] final commits: all MMAs retired
   uint64_t* dqbar = mma_done + kMmaWarps;   // bounded barrier of the dequant threads
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dqbar + 1);
+  uint64_t* rfull = dqbar + 1;   // csplit leader: every other split's partial arrived
+  uint64_t* rfree = rfull + 1;   // csplit non-leader: the leader consumed the receive buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfree + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(abort_flag) + 1;
 
@@ -542,6 +667,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     mbar_init(accempty, 1);
     for (int i = 0; i < kMmaWarps; ++i) mbar_init(&mma_done[i], 1);
     mbar_init(dqbar, kDqThreads);
+    mbar_init(rfull, (uint32_t)((p.splits - 1) * kDqWarps));
+    mbar_init(rfree, (uint32_t)kDqWarps);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -555,6 +682,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // every CTA's barriers are initialised before any CTA of the cluster arrives
+  // on them remotely
+  if constexpr (CSPLIT) cluster_sync();
   // accumulators: issuer i, chain c at columns (i * chains + c) * acc_cols; A ring after them
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_a = tmem + (uint32_t)(p.acc_cols * p.chains * p.issuers);
@@ -563,6 +693,13 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   // stages: sub-stages [ks0, ks1), ks0 a multiple of `sub`.
   const int units = p.n_tiles * p.m_tiles * p.splits;
   const int tstages = (p.kstages + sub - 1) / sub;
+  // Unit iteration: CTAs step through units by the grid size; with cluster
+  // split-K, the cluster steps through tiles and CTA rank r takes split r.
+  const int tiles_all = p.n_tiles * p.m_tiles;
+  const int crank = CSPLIT ? (int)cluster_rank() : 0;
+  const int u_first = CSPLIT ? (int)(blockIdx.x / p.splits) + tiles_all * crank : (int)blockIdx.x;
+  const int u_step = CSPLIT ? p.nclusters : (int)gridDim.x;
+  const int u_end = CSPLIT ? tiles_all * (crank + 1) : units;
   auto unit_range = [&](int u, int& nt, int& mt, int& ks0, int& ks1, int& sp) {
     nt = u % p.n_tiles;
     const int rest = u / p.n_tiles;
@@ -584,7 +721,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const uint32_t tbytes = p.t_kind == 1 ? (uint32_t)(2 * kTileN * 2 * sub)
                               : (p.t_kind == 2 ? (uint32_t)(p.t_rows * kBK * 4 * sub) : 0u);
       const int row_sub = w_sub_bytes / kTileN;
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+      for (int u = u_first; u < u_end && !*abort_flag; u += u_step) {
         int nt, mt, ks0, ks1, sp;
         unit_range(u, nt, mt, ks0, ks1, sp);
         for (int ks = ks0; ks < ks1; ks += sub, ++ti) {
@@ -641,7 +778,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       uint32_t a = 0, a_ph = 0;   // A ring slot and its phase parity
       int unit_i = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
+      for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
         int nt, mt, ks0, ks1, sp;
         unit_range(u, nt, mt, ks0, ks1, sp);
         if (!mbar_wait(accempty, (unit_i & 1) ^ 1, abort_flag)) {
@@ -721,7 +858,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       dq_ph ^= 1u;
       return done;
     };
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++unit_i) {
+    for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
       const int64_t n = (int64_t)nt * kTileN + row;
@@ -786,6 +923,16 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const Epi epi{p, rc, epoch, reduce};
       // accumulators holding this unit: issuers that took at least one sub-stage
       const int nacc = p.chains * min(p.issuers, ks1 - ks0);
+      constexpr bool csplit = CSPLIT;
+      // cluster split-K, non-leader: the leader must have consumed this
+      // cluster's previous tile from its receive buffer
+      if (csplit && crank > 0 && unit_i > 0 &&
+          !mbar_wait_cluster(rfree, (uint32_t)((unit_i - 1) & 1), abort_flag)) {
+        ok = false;
+        break;
+      }
+      float own[8];   // csplit leader: this thread's chunk of its own split
+      bool has_own = false;
       // this warp owns the 8-token column chunks c0 = 8 * (group + kGroups * i)
       for (int c0 = 8 * group; c0 < p.bn; c0 += 8 * kGroups) {
         float v[8];
@@ -796,17 +943,36 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[j] += w[j];
         }
-        if (split) {
+        if constexpr (csplit) {
+          if (crank > 0) {
+            // into the leader's receive buffer [split-1][token][row]
+            const uint32_t base = dsmem_map(
+                smem_u32(recv + ((crank - 1) * p.bn + c0) * kTileN + row), 0u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dsmem_st(base + (uint32_t)(j * kTileN * 4), v[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) own[j] = v[j];
+            has_own = true;
+          }
+        } else if (split) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int64_t m = m0 + c0 + j;
             if (m < p.M && n < p.N) p.ws[((int64_t)sp * p.M + m) * p.N + n] = v[j];
           }
-        } else {
+        }
+        if (!split) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[j] *= nscale;
           epi.emit8(m0 + c0, n, v, lane);
         }
+      }
+      if (csplit && crank > 0) {
+        // publish this warp's partial stores to the leader
+        fence_acq_rel_cluster();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(dsmem_map(smem_u32(rfull), 0u));
       }
       tc_fence_before();
       if (!dq_sync()) {
@@ -817,15 +983,44 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
       const int tile_id = mt * p.n_tiles + nt;
       bool finalize_here = !split;
-      if (split) {
-        // ticket: the last split to arrive sums all splits in split order
-        __threadfence();
+      if constexpr (csplit) {
+        finalize_here = crank == 0;
+        if (crank == 0) {
+          if (!mbar_wait_cluster(rfull, (uint32_t)(unit_i & 1), abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (has_own) {
+            // splits add in split order: own (split 0), then 1, 2, ...
+            const int c0 = 8 * group;
+            float acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = own[j];
+            for (int q = 1; q < p.splits; ++q) {
+              const float* part = recv + ((q - 1) * p.bn + c0) * kTileN + row;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[j] += part[j * kTileN];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] *= nscale;
+            epi.emit8(m0 + c0, n, acc, lane);
+          }
+          // hand the receive buffer back to every other split of the cluster
+          __syncwarp();
+          if (lane == 0)
+            for (int q = 1; q < p.splits; ++q) mbar_arrive_remote(dsmem_map(smem_u32(rfree), (uint32_t)q));
+        }
+      } else if (split) {   // global partials (only instantiated without CSPLIT)
+        // ticket: the last split to arrive sums all splits in split order.  The
+        // barrier orders every thread's partial stores before the ticket
+        // thread's release; its acquire (then the barrier) orders the
+        // finalizer's loads after every other split's release.
         if (!dq_sync()) {
           ok = false;
           break;
         }
         if (dt == 0) {
-          const uint32_t t = atomicAdd(&p.counters[tile_id], 1u);
+          const uint32_t t = ticket_add(&p.counters[tile_id]);
           *s_ticket = (t == (uint32_t)(p.splits - 1)) ? 1 : 0;
         }
         if (!dq_sync()) {
@@ -834,30 +1029,33 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
         finalize_here = *s_ticket != 0;
         if (finalize_here) {
-          __threadfence();
-          // same column ownership as above; the 8 tokens of a chunk load together
-          // (one L2 round trip per split), and splits add in split order
+          // same column ownership as above; the 8 tokens of a chunk and two
+          // splits at a time (plus, first, the residual) load together, and
+          // splits add in split order
           for (int c0 = 8 * group; c0 < p.bn; c0 += 8 * kGroups) {
-            float acc[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              const int64_t m = m0 + c0 + jj;
-              acc[jj] = (m < p.M && n < p.N) ? __ldcg(p.ws + m * p.N + n) : 0.0f;
-            }
-            for (int q = 1; q < p.splits; ++q) {
-              const float* part = p.ws + (int64_t)q * p.M * p.N;
-              float v[8];
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                const int64_t m = m0 + c0 + jj;
-                v[jj] = (m < p.M && n < p.N) ? __ldcg(part + m * p.N + n) : 0.0f;
+            float acc[8], res[8];
+            epi.load_res8(m0 + c0, n, lane, res);
+            for (int q0 = 0; q0 < p.splits; q0 += 2) {
+              float v[2][8];
+        #pragma unroll
+              for (int qq = 0; qq < 2; ++qq) {
+                const float* part = p.ws + (int64_t)(q0 + qq) * p.M * p.N;
+        #pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                  const int64_t m = m0 + c0 + jj;
+                  v[qq][jj] = (q0 + qq < p.splits && m < p.M && n < p.N) ? __ldcg(part + m * p.N + n)
+                                                                          : 0.0f;
+                }
               }
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) acc[jj] += v[jj];
+        #pragma unroll
+              for (int qq = 0; qq < 2; ++qq)
+        #pragma unroll
+                for (int jj = 0; jj < 8; ++jj)
+                  if (q0 + qq < p.splits) acc[jj] = (q0 + qq == 0) ? v[0][jj] : acc[jj] + v[qq][jj];
             }
-#pragma unroll
+        #pragma unroll
             for (int jj = 0; jj < 8; ++jj) acc[jj] *= nscale;
-            epi.emit8(m0 + c0, n, acc, lane);
+            epi.emit8(m0 + c0, n, acc, lane, res);
           }
           if (dt == 0) p.counters[tile_id] = 0u;
         }
@@ -879,6 +1077,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
   // ------------------------------ teardown ------------------------------
   __syncthreads();
+  // no CTA leaves while another CTA of its cluster may still write to its
+  // shared memory or arrive on its barriers
+  if constexpr (CSPLIT) cluster_sync();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -910,7 +1111,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         int64_t off[kPer], n[kPer], m[kPer];
         bool valid[kPer];
         float v[kPer];
-#pragma unroll
+  #pragma unroll
         for (int j = 0; j < kPer; ++j) {
           const int e = e0 + j * kThreads;
           n[j] = (int64_t)nt * kTileN + (e % kTileN);
@@ -919,27 +1120,29 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           off[j] = valid[j] ? m[j] * p.N + n[j] : 0;
           v[j] = valid[j] ? __ldcg(mine + off[j]) : 0.0f;
         }
+        const bool has_res = (p.epilogue & IE_EPI_RESIDUAL) != 0;
+        float r[kPer];
+  #pragma unroll
+        for (int j = 0; j < kPer; ++j)
+          r[j] = (has_res && valid[j]) ? load_val(p.residual, p.out_dtype, m[j] * p.ldr + n[j])
+                                       : 0.0f;
         for (int src = 1; src < rc.world; ++src) {
           const float* slot = mine + (int64_t)src * rc.slot_floats;
           float w[kPer];
-#pragma unroll
+  #pragma unroll
           for (int j = 0; j < kPer; ++j) w[j] = valid[j] ? __ldcg(slot + off[j]) : 0.0f;
-#pragma unroll
+  #pragma unroll
           for (int j = 0; j < kPer; ++j) v[j] += w[j];
         }
         if (p.epilogue & IE_EPI_BIAS) {
-#pragma unroll
+  #pragma unroll
           for (int j = 0; j < kPer; ++j) v[j] += valid[j] ? p.bias[n[j]] : 0.0f;
         }
-        if (p.epilogue & IE_EPI_RESIDUAL) {
-          float r[kPer];
-#pragma unroll
-          for (int j = 0; j < kPer; ++j)
-            r[j] = valid[j] ? load_val(p.residual, p.out_dtype, m[j] * p.ldr + n[j]) : 0.0f;
-#pragma unroll
+        if (has_res) {
+  #pragma unroll
           for (int j = 0; j < kPer; ++j) v[j] = r[j] + v[j];
         }
-#pragma unroll
+  #pragma unroll
         for (int j = 0; j < kPer; ++j)
           if (valid[j]) store_val(p.out, p.out_dtype, m[j] * p.ldo + n[j], v[j]);
       }
@@ -980,6 +1183,8 @@ struct Plan {
   size_t smem = 0;
   size_t ws_bytes = 0;       // counters + partials
   size_t counters_bytes = 0;
+  bool csplit = false;       // splits of a tile as one thread-block cluster
+  int recv_bytes = 0;
 };
 
 int sm_count() {
@@ -1023,6 +1228,13 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   double best = 1e300;
   const int tiles = pl.n_tiles * pl.m_tiles;
   const int tst = (pl.kstages + pl.sub - 1) / pl.sub;   // TMA stages along K
+  // Token tiles up to 32 tokens may also reduce their splits inside a cluster
+  // (2, 4 or 8 CTAs: those sizes pack the GPCs evenly, so a launch's clusters
+  // are all resident at once), which finalizes slightly sooner than global
+  // partials; each split count is scored both ways.
+  const bool cluster_ok = pl.bn <= 8 * kGroups;
+  constexpr double kClusterGain = 0.25;
+  bool best_cluster = false;
   for (int s = 1; s <= (allow_split ? 16 : 1); ++s) {
     if (s > 1 && tst < 2 * s) break;
     // every split must own at least one TMA stage: (s-1) * ceil(tst/s) < tst
@@ -1036,6 +1248,12 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
     if (t < best - 1e-9) {
       best = t;
       pl.splits = s;
+      best_cluster = false;
+    }
+    if (cluster_ok && (s == 2 || s == 4 || s == 8) && t - kClusterGain < best - 1e-9) {
+      best = t - kClusterGain;
+      pl.splits = s;
+      best_cluster = true;
     }
   }
   if (a.w.axis == IE_AXIS_GROUP128) {
@@ -1063,14 +1281,20 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   pl.tmem_cols = 32;
   while (pl.tmem_cols < accs + pl.na * kACols) pl.tmem_cols *= 2;
   const size_t x_stage = (size_t)pl.bn * kBK * 2 * pl.sub;
+  // Small token tiles: the splits of a tile run as one cluster and reduce
+  // through the leader's shared memory (receive buffer); no workspace.
+  if (pl.splits > 1 && best_cluster) {
+    pl.csplit = true;
+    pl.recv_bytes = (pl.splits - 1) * pl.bn * kTileN * 4;
+  }
   const size_t budget = 220 * 1024;
-  const size_t fixed = 1024 + 256;
+  const size_t fixed = 1024 + 256 + (size_t)pl.recv_bytes;
   const size_t per = x_stage + pl.w_stage_bytes + pl.t_stage_bytes;
   pl.ns = (int)std::min<size_t>(12, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
-  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 1) + 16;
+  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 3) + 16;
   if (pl.smem < (size_t)kMinSmem) pl.smem = kMinSmem;   // one CTA per SM: TMEM and co-residency
-  if (pl.splits > 1) {
+  if (pl.splits > 1 && !pl.csplit) {
     pl.counters_bytes = (((size_t)tiles * 4) + 255) / 256 * 256;
     pl.ws_bytes = pl.counters_bytes + (size_t)pl.splits * M * a.w.n * 4;
   }
@@ -1091,13 +1315,55 @@ template <int FMT>
 int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw,
                  const CUtensorMap& tx, const CUtensorMap& ts, const CUtensorMap& tz,
                  const TcParams& prm, const ReduceCtx* rc, cudaStream_t s) {
-  auto kern = qgemm_tc_kernel<FMT>;
+  auto kern = pl.csplit ? qgemm_tc_kernel<FMT, true> : qgemm_tc_kernel<FMT, false>;
   IE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)pl.smem));
   const int units = pl.n_tiles * pl.m_tiles * pl.splits;
-  const int grid = std::min(units, sm_count());
   ReduceCtx none{};
-  kern<<<grid, kThreads, pl.smem, s>>>(tw, tx, ts, tz, prm, rc ? *rc : none, rc ? 1 : 0);
+  const ReduceCtx ctx = rc ? *rc : none;
+  const int reduce = rc ? 1 : 0;
+  if (!pl.csplit) {
+    const int grid = std::min(units, sm_count());
+    kern<<<grid, kThreads, pl.smem, s>>>(tw, tx, ts, tz, prm, ctx, reduce);
+    return launch_status("qgemm_tc_kernel");
+  }
+  // cluster split-K: one cluster of `splits` CTAs per tile in flight, as many
+  // clusters as the device holds at once (every CTA co-resident, which the
+  // fused all-reduce relies on)
+  const int tiles = pl.n_tiles * pl.m_tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3((unsigned)kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)pl.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((unsigned)(tiles * pl.splits));
+  static std::mutex mu;
+  static int cached_key[4] = {-1, -1, -1, -1}, cached_max[4] = {0, 0, 0, 0};
+  int max_clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const int key = (int)pl.smem * 16 + pl.splits;
+    if (cached_key[FMT] == key) {
+      max_clusters = cached_max[FMT];
+    } else {
+      IE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, (const void*)kern, &cfg));
+      cached_key[FMT] = key;
+      cached_max[FMT] = max_clusters;
+    }
+  }
+  if (max_clusters <= 0)
+    return set_error(IE_ERR_UNSUPPORTED, "qlinear: no cluster of %d CTAs with %zu bytes of shared "
+                                         "memory fits on this device", pl.splits, pl.smem);
+  TcParams prm2 = prm;
+  prm2.nclusters = std::min(tiles, max_clusters);
+  cfg.gridDim = dim3((unsigned)(prm2.nclusters * pl.splits));
+  IE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, tz, prm2, ctx, reduce));
   return launch_status("qgemm_tc_kernel");
 }
 
@@ -1120,7 +1386,7 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   IE_CHECK(tc_eligible(a), "qlinear: the tensor-core path needs bf16/f16 activations, K %% 128 "
                            "== 0, 16-byte aligned rows and the driver's TMA encoder");
   Plan pl = make_plan(a, true);
-  if (pl.splits > 1 && (!a.workspace || a.workspace_bytes < pl.ws_bytes)) pl = make_plan(a, false);
+  if (pl.ws_bytes > 0 && (!a.workspace || a.workspace_bytes < pl.ws_bytes)) pl = make_plan(a, false);
   EncodeFn enc = encode_fn();
   CUtensorMap tw, tx;
   {
@@ -1219,7 +1485,9 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   prm.t_stage_bytes = pl.t_stage_bytes;
   prm.t_joint = joint ? 1 : 0;
   prm.sub = pl.sub;
-  if (pl.splits > 1) {
+  prm.csplit = pl.csplit ? 1 : 0;
+  prm.recv_bytes = pl.recv_bytes;
+  if (pl.splits > 1 && !pl.csplit) {
     prm.counters = static_cast<uint32_t*>(a.workspace);
     prm.ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pl.counters_bytes);
   }

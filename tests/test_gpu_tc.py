@@ -122,4 +122,7 @@ def test_auto_routes_decode_batches_to_the_tensor_cores():
     x = torch.from_numpy(o.seeded_activations(8, 1024, seed=51)).cuda().to(torch.bfloat16)
     assert torch.equal(qlinear(x, p), qlinear(x, p, algo=ALGO_TCGEN05))
     x1 = x[:1]
-    assert torch.equal(qlinear(x1, p), qlinear(x1, p, algo=ALGO_GEMV))
+    assert torch.equal(qlinear(x1, p), qlinear(x1, p, algo=ALGO_TCGEN05))
+    # f32 activations stay on the weight-streaming kernel
+    xf = x1.float()
+    assert torch.equal(qlinear(xf, p), qlinear(xf, p, algo=ALGO_GEMV))
