@@ -5,8 +5,9 @@
 
 Workload (the int4 Llama-3-8B-shaped decoder): one
 decode step of the whole model's quantized linear path -- 32 layers x
-{rms_norm, qkv (column), o (row + fused all-reduce + residual), rms_norm,
-gate/up (column, fused SiLU*up), down (row + fused all-reduce + residual)} --
+{rms_norm + qkv (column; the norm folded into the GEMM), o (row + fused
+all-reduce + residual), rms_norm + gate/up (column, folded norm, fused
+SiLU*up), down (row + fused all-reduce + residual)} --
 for a decode batch of 16 tokens, int4 asymmetric group-128 weights (f16
 scales/zeros), bf16 activations, tensor-parallel over N GPUs (TP=N, total work
 fixed: strong scaling).  Attention is outside the path (see ie_tpq.stack).
@@ -51,6 +52,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--scheme", default="int4-g128")
+    ap.add_argument("--unfused-norm", action="store_true",
+                    help="run each rms_norm as its own kernel instead of inside the next GEMM")
     return ap.parse_args()
 
 
@@ -244,7 +247,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                             timeout_s=10.0)
     layers = [synthetic_layer(shape, args.scheme, shard, seed=1000 + li)
               for li in range(args.layers)]
-    stack = LinearStack(shape, layers, args.batch, torch.bfloat16, comm=comm, world=world)
+    stack = LinearStack(shape, layers, args.batch, torch.bfloat16, comm=comm, world=world,
+                        fuse_norm=not args.unfused_norm)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(7)
     stack.x_in.copy_(torch.randn(stack.x_in.shape, generator=gen, device="cuda"))

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define IE_TPQ_ABI_VERSION 1
+#define IE_TPQ_ABI_VERSION 2   /* 2: ie_qlinear_args gained norm_weight / norm_eps */
 
 /* ---- status codes --------------------------------------------------- */
 #define IE_OK 0
@@ -62,6 +62,11 @@ extern "C" {
 #define IE_EPI_BIAS 1        /* out += bias[n] (f32), added once after any reduction */
 #define IE_EPI_RESIDUAL 2    /* out = residual + (...), residual has out's dtype      */
 #define IE_EPI_SILU_MUL 4    /* rows are gate/up pairs: out[:, j] = silu(row 2j) * row 2j+1 */
+/* Prologue: x is RMS-normalised first, x -> x / sqrt(mean_k(x^2) + norm_eps) * norm_weight
+ * (ie/layers/functional.py:6-8; ie/kernels/torch_backend.py:103-105 before the qkv and
+ * gate/up projections), folded into the tensor-core kernel: bf16/f16 x only, otherwise
+ * IE_ERR_UNSUPPORTED (IE_ERR_INVALID with algo = 1). */
+#define IE_EPI_RMS_NORM 8
 
 /* ---- packed weight ------------------------------------------------------ */
 typedef struct ie_qweight {
@@ -96,6 +101,9 @@ typedef struct ie_qlinear_args {
                            (bf16/f16 activations, K % 128 == 0, 16-byte aligned rows) */
   void* workspace;      /* caller-owned scratch (see ie_qlinear_workspace_size), may be NULL */
   size_t workspace_bytes;
+  const float* norm_weight;  /* IE_EPI_RMS_NORM: f32 [k], 16-byte aligned */
+  float norm_eps;
+  int32_t reserved;
 } ie_qlinear_args;
 
 /* ---- library ------------------------------------------------------------ */

@@ -46,8 +46,14 @@ int validate_linear(const ie_qlinear_args& a) {
     IE_CHECK(a.residual, "qlinear: RESIDUAL flag without a residual pointer");
     IE_CHECK(a.ldr >= ncols, "qlinear: ldr %lld < output columns", (long long)a.ldr);
   }
-  IE_CHECK((a.epilogue & ~(IE_EPI_BIAS | IE_EPI_RESIDUAL | IE_EPI_SILU_MUL)) == 0,
+  IE_CHECK((a.epilogue & ~(IE_EPI_BIAS | IE_EPI_RESIDUAL | IE_EPI_SILU_MUL | IE_EPI_RMS_NORM)) ==
+               0,
            "qlinear: unknown epilogue flags 0x%x", a.epilogue);
+  if (a.epilogue & IE_EPI_RMS_NORM) {
+    IE_CHECK(a.norm_weight, "qlinear: RMS_NORM flag without a norm weight");
+    IE_CHECK(a.norm_eps >= 0.0f, "qlinear: negative norm eps");
+    IE_CHECK(a.algo != 1, "qlinear: the fused RMS norm runs on the tensor-core path only");
+  }
   IE_CHECK(a.algo >= 0 && a.algo <= 2, "qlinear: unknown algo %d", a.algo);
   return IE_OK;
 }
@@ -88,6 +94,9 @@ extern "C" int ie_qlinear(const ie_qlinear_args* a, void* stream) {
   int rc = validate_linear(*a);
   if (rc || a->m == 0) return rc;
   if (use_tc(*a)) return launch_qlinear_tc(*a, nullptr, as_stream(stream));
+  if (a->epilogue & IE_EPI_RMS_NORM)
+    return set_error(IE_ERR_UNSUPPORTED, "qlinear: the fused RMS norm needs bf16/f16 "
+                                         "activations, K %% 128 == 0 and aligned rows");
   return launch_qlinear_gemv(*a, nullptr, 0, as_stream(stream));
 }
 
@@ -117,6 +126,9 @@ extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* 
     if (rc) return rc;
     return launch_qlinear_tc(*a, &ctx, as_stream(stream));
   }
+  if (a->epilogue & IE_EPI_RMS_NORM)
+    return set_error(IE_ERR_UNSUPPORTED, "qlinear_allreduce: the fused RMS norm needs bf16/f16 "
+                                         "activations, K %% 128 == 0 and aligned rows");
   int resident = 0;
   rc = gemv_resident_ctas(*a, &resident);
   if (rc) return rc;

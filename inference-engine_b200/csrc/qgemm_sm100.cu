@@ -102,6 +102,13 @@ struct TcParams {
   int recv_bytes;           // csplit: leader's receive buffer [splits-1][bn][128] f32
   float* ws;                // split-K partials [splits][M][N]
   uint32_t* counters;       // per (m_tile, n_tile) tickets, self-resetting
+  // RMS-norm prologue: x rows (plain loads for the per-token sum of squares)
+  // and the f32 weight over K; the x tiles are scaled while they are converted
+  const void* x;
+  int64_t ldx;
+  const float* norm_w;      // null: no prologue
+  float norm_eps;
+  int nw_off;               // byte offset of a stage's norm weights [sub][128] in its table slot
 };
 
 // ---------------------------------------------------------------------------
@@ -162,6 +169,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// Plain (untiled) bulk copy of `bytes` (a multiple of 16, both addresses
+// 16-byte aligned) into this CTA's shared memory.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
@@ -541,6 +558,87 @@ __device__ __forceinline__ void bf16_to_f16_chunk(uint4* p) {
   *p = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Packed f32 pairs: Blackwell multiplies two f32 lanes per instruction.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t f32x2_to_h2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return pack_h2(lo, hi);
+}
+
+// RMS-norm prologue, one 16-byte chunk of the x tile (8 consecutive K of one
+// token): f16((x * rinv) * w), with rinv = 1 / sqrt(mean(x^2) + eps) of the
+// token; each product rounded to f32 (round to nearest), two lanes per
+// instruction.  The 8 weights come from the stage's copy in shared memory.
+template <bool XBF16>
+__device__ __forceinline__ void norm_chunk(uint4* p, const float* w8, float rinv) {
+  const uint4 v = *p;
+  const ulonglong2 wa = reinterpret_cast<const ulonglong2*>(w8)[0];
+  const ulonglong2 wb = reinterpret_cast<const ulonglong2*>(w8)[1];
+  const uint64_t wv[4] = {wa.x, wa.y, wb.x, wb.y};
+  const uint64_t rr = f32x2(rinv, rinv);
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint64_t xv;
+    if constexpr (XBF16) {
+      xv = f32x2(__uint_as_float(u[i] << 16), __uint_as_float(u[i] & 0xFFFF0000u));
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+      xv = f32x2(f.x, f.y);
+    }
+    o[i] = f32x2_to_h2(mul_f32x2(mul_f32x2(xv, rr), wv[i]));
+  }
+  *p = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Sum of squares of one K-long row of x by one warp: 16-byte loads, sixteen
+// in flight per lane (a 4096-wide row in one round trip), then a butterfly;
+// the same order on every call.
+constexpr int kSumsqLoads = 8;
+__device__ __forceinline__ float row_sumsq(const void* row, int64_t K, int x_bf16, int lane) {
+  float ss = 0.0f;
+  const uint4* r = static_cast<const uint4*>(row);   // 8 elements per uint4
+  const int64_t chunks = K / 8;
+  for (int64_t c0 = lane; c0 < chunks; c0 += 32 * kSumsqLoads) {
+    uint4 v[kSumsqLoads];
+#pragma unroll
+    for (int j = 0; j < kSumsqLoads; ++j)
+      v[j] = c0 + 32 * j < chunks ? __ldcg(r + c0 + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < kSumsqLoads; ++j) {
+      const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo, hi;
+        if (x_bf16) {
+          lo = __uint_as_float(u[i] << 16);
+          hi = __uint_as_float(u[i] & 0xFFFF0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+          lo = f.x;
+          hi = f.y;
+        }
+        ss = fmaf(lo, lo, ss);
+        ss = fmaf(hi, hi, ss);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  return ss;
+}
+
 // Epilogue value of token m, row n, before the residual: scale, then bias.
 struct Epi {
   const TcParams& p;
@@ -650,6 +748,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfree + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(abort_flag) + 1;
+  float* s_rinv = reinterpret_cast<float*>(s_ticket + 1);   // [bn] RMS-norm prologue
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t epoch = reduce ? reduce_epoch(rc) : 0u;
@@ -730,7 +829,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             *abort_flag = 1;
             break;
           }
-          mbar_expect_tx(&full[s], (uint32_t)(p.w_stage_bytes + x_stage_bytes) + tbytes);
+          const uint32_t nbytes = p.norm_w ? (uint32_t)(min(sub, p.kstages - ks) * kBK * 4) : 0u;
+          mbar_expect_tx(&full[s], (uint32_t)(p.w_stage_bytes + x_stage_bytes) + tbytes + nbytes);
           uint8_t* ws_ = w_ring + s * p.w_stage_bytes;
           for (int j = 0; j < sub; ++j)   // K past the end reads as zeros
             tma_load_2d(ws_ + j * w_sub_bytes, &tm_w, (ks + j) * row_sub, nt * kTileN, &full[s]);
@@ -745,6 +845,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           } else if (p.t_kind == 2) {
             tma_load_3d(ts, &tm_s, 0, ks, 0, &full[s]);               // [rows][sub][128]
           }
+          if (p.norm_w)   // the stage's norm weights, only those inside [0, K)
+            bulk_load(ts + p.nw_off, p.norm_w + (int64_t)ks * kBK,
+                      (uint32_t)(min(sub, p.kstages - ks) * kBK * 4), &full[s]);
           // every 64-wide K block of the stage's activation tile in one copy
           tma_load_3d(x_ring + s * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[s]);
         }
@@ -858,10 +961,32 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       dq_ph ^= 1u;
       return done;
     };
+    int norm_mt = -1;   // token tile whose RMS factors s_rinv holds
     for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
       const int64_t n = (int64_t)nt * kTileN + row;
+      if (p.norm_w && mt != norm_mt) {
+        // RMS factors of the tile's tokens over the full K (every split needs
+        // them, so each CTA reads the rows itself, from L2): dequant warp w
+        // takes tokens w, w + 16, ...  The previous unit's conversions all
+        // finished before its epilogue barrier, so s_rinv is free to rewrite.
+        norm_mt = mt;
+        for (int t = warp - kDqWarp0; t < p.bn; t += kDqWarps) {
+          const int64_t m = (int64_t)mt * p.bn + t;
+          float rinv = 0.0f;
+          if (m < p.M) {
+            const float ss = row_sumsq(static_cast<const char*>(p.x) + m * p.ldx * 2, p.K,
+                                       p.x_bf16, lane);
+            rinv = 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.norm_eps));
+          }
+          if (lane == 0) s_rinv[t] = rinv;
+        }
+        if (!dq_sync()) {
+          ok = false;
+          break;
+        }
+      }
       int lsub = 0;   // sub-stage index within the unit; pair lsub % kPairs takes it
       for (int ks = ks0; ks < ks1 && ok; ks += sub) {
         const int nsub = min(sub, ks1 - ks);
@@ -882,7 +1007,24 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             uint32_t o[32];
             dequant_half<FMT>(wst, row, half, tst, p.t_rows, p.axis, n, j, sub, o);
             tmem_st32(tmem_a + lane_addr + a * (uint32_t)kACols + (uint32_t)(half * 32), o);
-            if (p.x_bf16) {
+            if (p.norm_w) {
+              // chunk i of the sub-stage: 128-byte line i / 8 = (64-K block,
+              // token), 16-byte column (i % 8) XOR (line % 8) under the
+              // 128-byte swizzle (bn is a multiple of 16, so line % 8 is the
+              // token's); every chunk of a TMA stage lies inside [0, K)
+              uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
+              const float* wk =
+                  reinterpret_cast<const float*>(t_ring + s * p.t_stage_bytes + p.nw_off) + j * kBK;
+              for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) {
+                const int line = i >> 3;                 // < 2 * bn
+                const bool hi = line >= p.bn;            // second 64-K block
+                const int t = hi ? line - p.bn : line;
+                const int kof = (hi ? 64 : 0) + (((i & 7) ^ (line & 7)) << 3);
+                if (p.x_bf16) norm_chunk<true>(xs + i, wk + kof, s_rinv[t]);
+                else norm_chunk<false>(xs + i, wk + kof, s_rinv[t]);
+              }
+              fence_proxy_async();
+            } else if (p.x_bf16) {
               uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
               for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) bf16_to_f16_chunk(xs + i);
               fence_proxy_async();
@@ -1179,7 +1321,7 @@ struct Plan {
   int fmt = 0, bn = 16, m_tiles = 1, n_tiles = 1, splits = 1, kstages = 1, ns = 2, na = 2;
   int acc_cols = 32, chains = 1, issuers = 1, tmem_cols = 512, sub = 1;
   int w_stage_bytes = 0;
-  int t_kind = 0, t_rows = 0, t_stage_bytes = 0;
+  int t_kind = 0, t_rows = 0, t_stage_bytes = 0, nw_off = 0;
   size_t smem = 0;
   size_t ws_bytes = 0;       // counters + partials
   size_t counters_bytes = 0;
@@ -1256,14 +1398,19 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
       best_cluster = true;
     }
   }
+  int tbytes = 0;   // table bytes of a stage
   if (a.w.axis == IE_AXIS_GROUP128) {
     pl.t_kind = 1;
-    pl.t_stage_bytes = ((2 * kTileN * 2 * pl.sub + 1023) / 1024) * 1024;
+    tbytes = 2 * kTileN * 2 * pl.sub;
   } else if (a.w.axis == IE_AXIS_K) {
     pl.t_kind = 2;
     pl.t_rows = a.w.gate_up ? 2 : 1;
-    pl.t_stage_bytes = ((pl.t_rows * kBK * 4 * pl.sub + 1023) / 1024) * 1024;
+    tbytes = pl.t_rows * kBK * 4 * pl.sub;
   }
+  // the RMS-norm weights of a stage follow its tables in the same slot
+  pl.nw_off = (tbytes + 15) / 16 * 16;
+  if (a.epilogue & IE_EPI_RMS_NORM) tbytes = pl.nw_off + kBK * 4 * pl.sub;
+  pl.t_stage_bytes = (tbytes + 1023) / 1024 * 1024;
   // TMEM: accumulators, then the A ring (64 columns a sub-stage).  Narrow token
   // tiles rotate their MMAs over independent accumulator chains, and two issuing
   // threads take alternate sub-stages into separate accumulators whenever TMEM
@@ -1292,7 +1439,9 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   const size_t per = x_stage + pl.w_stage_bytes + pl.t_stage_bytes;
   pl.ns = (int)std::min<size_t>(12, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
-  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 3) + 16;
+  // barriers, then TMEM slot, abort flag, ticket and the RMS factors [bn]
+  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 3) + 16 +
+            4 * (size_t)pl.bn;
   if (pl.smem < (size_t)kMinSmem) pl.smem = kMinSmem;   // one CTA per SM: TMEM and co-residency
   if (pl.splits > 1 && !pl.csplit) {
     pl.counters_bytes = (((size_t)tiles * 4) + 255) / 256 * 256;
@@ -1308,6 +1457,7 @@ bool tc_eligible(const ie_qlinear_args& a) {
   if (((uintptr_t)a.w.codes & 15)) return false;
   if (((uintptr_t)a.w.scale & 15)) return false;
   if (a.w.axis == IE_AXIS_GROUP128 && ((a.w.n % 8) || ((uintptr_t)a.w.zero & 15))) return false;
+  if ((a.epilogue & IE_EPI_RMS_NORM) && ((uintptr_t)a.norm_weight & 15)) return false;
   return encode_fn() != nullptr;
 }
 
@@ -1384,7 +1534,8 @@ int64_t tc_tiles(const ie_qlinear_args& a) {
 int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_t s) {
   using namespace tc;
   IE_CHECK(tc_eligible(a), "qlinear: the tensor-core path needs bf16/f16 activations, K %% 128 "
-                           "== 0, 16-byte aligned rows and the driver's TMA encoder");
+                           "== 0, 16-byte aligned rows (and norm weight) and the driver's TMA "
+                           "encoder");
   Plan pl = make_plan(a, true);
   if (pl.ws_bytes > 0 && (!a.workspace || a.workspace_bytes < pl.ws_bytes)) pl = make_plan(a, false);
   EncodeFn enc = encode_fn();
@@ -1492,6 +1643,13 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
     prm.ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pl.counters_bytes);
   }
   prm.x_bf16 = a.act_dtype == IE_DT_BF16 ? 1 : 0;
+  if (a.epilogue & IE_EPI_RMS_NORM) {
+    prm.x = a.x;
+    prm.ldx = a.ldx;
+    prm.norm_w = a.norm_weight;
+    prm.norm_eps = a.norm_eps;
+    prm.nw_off = pl.nw_off;
+  }
   switch (pl.fmt) {
     case F_INT4G: return launch_typed<F_INT4G>(a, pl, tw, tx, ts, tz, prm, rc, s);
     case F_INT4SYM: return launch_typed<F_INT4SYM>(a, pl, tw, tx, ts, tz, prm, rc, s);

@@ -38,6 +38,7 @@ IE_DT_U8 = 4
 IE_EPI_BIAS = 1
 IE_EPI_RESIDUAL = 2
 IE_EPI_SILU_MUL = 4
+IE_EPI_RMS_NORM = 8
 
 IE_COMM_HANDLE_BYTES = 64
 IE_QLINEAR_NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -85,6 +86,9 @@ class QLinearArgs(ctypes.Structure):
         ("algo", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
     ]
 
 

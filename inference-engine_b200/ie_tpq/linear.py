@@ -32,8 +32,31 @@ def shared_workspace(nbytes: int, device):
     return ws
 
 
+# Largest token batch for which folding the RMS norm into the next GEMM beats
+# a separate rms_norm launch.  Each CTA of the fused call first reads its token
+# rows from L2 for the sums of squares and then scales every x tile it
+# converts; on B200 with Llama-3-8B shapes (qkv + gate/up, int4-g128) the
+# two fused calls cost 3.6 / 4.6 us more than the plain GEMMs at 8 / 16 tokens
+# against 6.8 / 7.2 us for two rms_norm launches, and 10.6 us more at 24-32.
+FUSED_NORM_MAX_TOKENS = 16
+
+
+def fused_norm_ok(x, w: PackedWeight) -> bool:
+    """Whether ``qlinear(x, w, norm_weight=...)`` can fold the RMS norm in:
+    the tensor-core path (bf16/f16 rows, 16-byte aligned, K a multiple of 128)."""
+    torch = require_cuda()
+    return (x.dim() == 2 and x.dtype in (torch.bfloat16, torch.float16) and w.k % 128 == 0
+            and x.stride(1) == 1 and x.data_ptr() % 16 == 0 and (x.stride(0) * 2) % 16 == 0)
+
+
+def fuse_norm_pays(x, w: PackedWeight) -> bool:
+    """``fused_norm_ok`` and a batch small enough for the fold to be faster."""
+    return x.shape[0] <= FUSED_NORM_MAX_TOKENS and fused_norm_ok(x, w)
+
+
 def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=False,
-               algo=ALGO_AUTO, workspace=None) -> _lib.QLinearArgs:
+               algo=ALGO_AUTO, workspace=None, norm_weight=None,
+               norm_eps: float = 1e-6) -> _lib.QLinearArgs:
     if x.dim() != 2:
         raise ValueError(f"x must be 2-D [tokens, K], got shape {tuple(x.shape)}")
     if x.shape[1] != w.k:
@@ -49,6 +72,11 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
             raise ValueError("residual must match out's dtype and be row-contiguous")
     if silu_mul:
         epi |= _lib.IE_EPI_SILU_MUL
+    if norm_weight is not None:
+        epi |= _lib.IE_EPI_RMS_NORM
+        if norm_weight.dtype != require_cuda().float32 or norm_weight.numel() != w.k or \
+                not norm_weight.is_contiguous():
+            raise ValueError(f"norm_weight must be a contiguous f32 [{w.k}] tensor")
     a = _lib.QLinearArgs()
     a.w = w.qweight()
     a.m = x.shape[0]
@@ -62,6 +90,8 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
     a.residual = residual.data_ptr() if residual is not None else None
     a.ldr = residual.stride(0) if residual is not None else 0
     a.epilogue = epi
+    a.norm_weight = norm_weight.data_ptr() if norm_weight is not None else None
+    a.norm_eps = float(norm_eps)
     a.algo = algo
     a.workspace = workspace.data_ptr() if workspace is not None else None
     a.workspace_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
@@ -70,12 +100,15 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
 
 def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | None = None,
             out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None,
-            workspace=None):
+            workspace=None, norm_weight=None, norm_eps: float = 1e-6):
     """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce.
 
     x: CUDA tensor ``[M, K]`` (bf16 / f16 / f32).  bias: f32 ``[N]``.  residual:
     ``[M, N]`` of the output dtype, added after the reduction.  A gate/up pair
-    weight returns ``silu(gate) * up`` of shape ``[M, N/2]``.
+    weight returns ``silu(gate) * up`` of shape ``[M, N/2]``.  ``norm_weight``
+    (f32 ``[K]``) folds ``rms_norm(x, norm_weight, norm_eps)`` in front of the
+    product (ie/layers/functional.py:6-8); it needs the tensor-core path
+    (``fused_norm_ok``) and raises otherwise.
     """
     torch = require_cuda()
     if silu_mul is None:
@@ -86,7 +119,11 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
         out = torch.empty((x.shape[0], cols), dtype=out_dtype, device=x.device)
     if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
         bias = bias.to(torch.float32).contiguous()
-    a = build_args(x, w, out, bias=bias, residual=residual, silu_mul=silu_mul, algo=algo)
+    if norm_weight is not None and (norm_weight.dtype != torch.float32
+                                    or not norm_weight.is_contiguous()):
+        norm_weight = norm_weight.to(torch.float32).contiguous()
+    a = build_args(x, w, out, bias=bias, residual=residual, silu_mul=silu_mul, algo=algo,
+                   norm_weight=norm_weight, norm_eps=norm_eps)
     need = _lib.lib().ie_qlinear_workspace_size(ctypes.byref(a))
     if need:
         ws = workspace if workspace is not None else shared_workspace(need, x.device)

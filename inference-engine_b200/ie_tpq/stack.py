@@ -24,7 +24,7 @@ from dataclasses import dataclass
 
 from . import _lib
 from .device import require_cuda
-from .linear import qlinear
+from .linear import fuse_norm_pays, qlinear
 from .packed import PackedWeight, concat_rows, quantize_on_device
 from .sharding import Shard
 from .tensor_parallel import rms_norm
@@ -115,7 +115,7 @@ class LinearStack:
     """The linear path of ``len(layers)`` decoder layers for one TP rank."""
 
     def __init__(self, shape: DecoderShape, layers: list[dict], batch: int, dtype=None,
-                 comm=None, world: int = 1):
+                 comm=None, world: int = 1, fuse_norm: bool = True):
         torch = require_cuda()
         self.shape = shape
         self.layers = layers
@@ -129,32 +129,43 @@ class LinearStack:
         self.x_out = torch.zeros((batch, h), dtype=self.dtype, device="cuda")
         self.graph = None
         self.launches_per_step = 0
+        # fold each rms_norm into the column-parallel GEMM that consumes it
+        self.fuse_norm = fuse_norm
 
     def _row(self, a, w, residual):
         if self.comm is not None and self.world > 1:
             return qlinear(a, w, residual=residual, comm=self.comm)
         return qlinear(a, w, residual=residual)
 
+    def _norm(self, x, w):
+        """(input, norm weight) for the GEMM after a norm: x itself and the
+        weight when the GEMM folds the norm in, else the normalised x."""
+        if self.fuse_norm and fuse_norm_pays(x, w):
+            return x, self.norm
+        return rms_norm(x, self.norm), None
+
     def forward(self, x):
         """One decode step over all layers; returns the new hidden state."""
         q_cols = self.shape.q_out // self.world
         launches = 0
         for layer in self.layers:
-            h = rms_norm(x, self.norm)
+            first = layer["qkv"] if "qkv" in layer else layer["q"]
+            h, nw = self._norm(x, first)
+            launches += nw is None
             if "qkv" in layer:
-                qkv = qlinear(h, layer["qkv"])
+                qkv = qlinear(h, layer["qkv"], norm_weight=nw)
                 a = qkv[:, :q_cols]
-                launches += 2
+                launches += 1
             else:
-                a = qlinear(h, layer["q"])
-                qlinear(h, layer["k"])
-                qlinear(h, layer["v"])
-                launches += 4
+                a = qlinear(h, layer["q"], norm_weight=nw)
+                qlinear(h, layer["k"], norm_weight=nw)
+                qlinear(h, layer["v"], norm_weight=nw)
+                launches += 3
             x = self._row(a, layer["o"], x)
-            h = rms_norm(x, self.norm)
-            u = qlinear(h, layer["gate_up"])
+            h, nw = self._norm(x, layer["gate_up"])
+            u = qlinear(h, layer["gate_up"], norm_weight=nw)
             x = self._row(u, layer["down"], x)
-            launches += 4
+            launches += 3 + (nw is None)
         self.launches_per_step = launches
         return x
 

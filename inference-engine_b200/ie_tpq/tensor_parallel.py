@@ -69,10 +69,13 @@ class ShardedMLP:
 
     def forward(self, x, comm=None):
         """Partial ``(silu(n@g) * (n@u)) @ d`` (comm=None), or ``x + sum of partials``."""
-        from .linear import qlinear
+        from .linear import fuse_norm_pays, qlinear
 
-        normed = rms_norm(x, self.norm, self.eps)
-        hidden = qlinear(normed, self.gate_up, silu_mul=True)
+        if fuse_norm_pays(x, self.gate_up):
+            hidden = qlinear(x, self.gate_up, silu_mul=True, norm_weight=self.norm,
+                             norm_eps=self.eps)
+        else:
+            hidden = qlinear(rms_norm(x, self.norm, self.eps), self.gate_up, silu_mul=True)
         if comm is None:
             return qlinear(hidden, self.down, out_dtype=x.dtype)
         return qlinear(hidden, self.down, residual=x, comm=comm, out_dtype=x.dtype)

@@ -86,6 +86,21 @@ def test_gate_up_pair_with_silu():
     assert status_bits() == 0
 
 
+def test_fused_rms_norm():
+    k, n, m = 4096, 1024, 64
+    p = W.quantize_grouped(o.seeded_weight(k, n, seed=11)).packed()
+    x = torch.from_numpy(o.seeded_activations(m, k, seed=12) * 4).cuda().to(torch.bfloat16)
+    nw = torch.linspace(0.5, 1.5, k, device="cuda")
+    want = qlinear(x, p, norm_weight=nw, algo=ALGO_TCGEN05)
+    for _ in range(2):
+        out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        a = build_args(x, p, out, norm_weight=nw, algo=ALGO_TCGEN05)
+        assert split_k_bytes(a) > 0
+        _lib.check(noalloc(a), "qlinear_noalloc")
+        assert torch.equal(out, want)
+    assert status_bits() == 0
+
+
 def test_plans_beyond_the_static_scratch_are_rejected():
     k, n, m = 8192, 4096, 256
     p = W.quantize_grouped(o.seeded_weight(k, n, seed=9)).packed()
