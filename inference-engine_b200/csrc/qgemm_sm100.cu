@@ -723,8 +723,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
                 const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                 TcParams p, ReduceCtx rc, int reduce) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base, derived from smem_raw by pointer arithmetic so that
+  // the compiler still knows every derived pointer is shared memory (a round
+  // trip through an integer would turn their accesses into generic ones)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int ns = p.ns, na = p.na, sub = p.sub;
   // one TMA stage = `sub` consecutive 128-K sub-stages behind one full/empty pair
   const int w_sub_bytes = p.w_stage_bytes / sub;           // [128 rows][row bytes] per sub
