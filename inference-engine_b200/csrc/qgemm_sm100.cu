@@ -902,29 +902,37 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             ok = false;
             break;
           }
-          for (int j = 0; j < nsub; ++j, ++lsub) {
-            if (p.issuers == 1 || (lsub & 1) == issuer) {
-              // afull implies the stage's TMA landed: the dequant warps waited on it
-              if (!mbar_wait(&afull[a], a_ph, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t a_col = tmem_a + a * (uint32_t)kACols;
-              const uint32_t xb = x_lo + (uint32_t)j * x_sub16;
+          // this issuer's sub-stages of the stage, j = first, first + issuers, ...;
+          // sub-stage j uses A slot (a + j) mod na
+          const int first = p.issuers == 1 ? 0 : (issuer ^ (lsub & 1));
+          for (int j = first; j < nsub; j += p.issuers) {
+            uint32_t aj = a + (uint32_t)j, phj = a_ph;
+            while (aj >= (uint32_t)na) {
+              aj -= (uint32_t)na;
+              phj ^= 1u;
+            }
+            // afull implies the stage's TMA landed: the dequant warps waited on it
+            if (!mbar_wait(&afull[aj], phj, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_col = tmem_a + aj * (uint32_t)kACols;
+            const uint32_t xb = x_lo + (uint32_t)j * x_sub16;
 #pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)
-                tc_mma_ts(dcol[kk], a_col + (uint32_t)(kk * 8), sw128_desc_from(xb + boff[kk]),
-                          idesc, (mask >> kk) & 1u);
-              mask = 0xFFu;
-              tc_commit(&aempty[a]);
-            }
-            if (++a == (uint32_t)na) {
-              a = 0;
-              a_ph ^= 1u;
-            }
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              tc_mma_ts(dcol[kk], a_col + (uint32_t)(kk * 8), sw128_desc_from(xb + boff[kk]),
+                        idesc, (mask >> kk) & 1u);
+            mask = 0xFFu;
+            tc_commit(&aempty[aj]);
           }
           if (!ok) break;
+          lsub += nsub;
+          a += (uint32_t)nsub;
+          while (a >= (uint32_t)na) {
+            a -= (uint32_t)na;
+            a_ph ^= 1u;
+          }
           tc_commit(&empty[s]);
           if (++s == (uint32_t)ns) {
             s = 0;
@@ -998,50 +1006,58 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           ok = false;
           break;
         }
-        for (int j = 0; j < nsub; ++j, ++lsub) {
-          if (lsub % kPairs == pair) {
-            if (!mbar_wait(&aempty[a], a_ph ^ 1u, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint8_t* wst = w_ring + s * p.w_stage_bytes + j * w_sub_bytes;
-            const uint8_t* tst = t_ring + s * p.t_stage_bytes;
-            uint32_t o[32];
-            dequant_half<FMT>(wst, row, half, tst, p.t_rows, p.axis, n, j, sub, o);
-            tmem_st32(tmem_a + lane_addr + a * (uint32_t)kACols + (uint32_t)(half * 32), o);
-            if (p.norm_w) {
-              // chunk i of the sub-stage: 128-byte line i / 8 = (64-K block,
-              // token), 16-byte column (i % 8) XOR (line % 8) under the
-              // 128-byte swizzle (bn is a multiple of 16, so line % 8 is the
-              // token's); every chunk of a TMA stage lies inside [0, K)
-              uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
-              const float* wk =
-                  reinterpret_cast<const float*>(t_ring + s * p.t_stage_bytes + p.nw_off) + j * kBK;
-              for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) {
-                const int line = i >> 3;                 // < 2 * bn
-                const bool hi = line >= p.bn;            // second 64-K block
-                const int t = hi ? line - p.bn : line;
-                const int kof = (hi ? 64 : 0) + (((i & 7) ^ (line & 7)) << 3);
-                if (p.x_bf16) norm_chunk<true>(xs + i, wk + kof, s_rinv[t]);
-                else norm_chunk<false>(xs + i, wk + kof, s_rinv[t]);
-              }
-              fence_proxy_async();
-            } else if (p.x_bf16) {
-              uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
-              for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) bf16_to_f16_chunk(xs + i);
-              fence_proxy_async();
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&afull[a]);
+        // this pair's sub-stages of the stage: j = first, first + kPairs, ...;
+        // sub-stage j uses A slot (a + j) mod na
+        const int first = (pair - lsub % kPairs + kPairs) % kPairs;
+        for (int j = first; j < nsub; j += kPairs) {
+          uint32_t aj = a + (uint32_t)j, phj = a_ph;
+          while (aj >= (uint32_t)na) {
+            aj -= (uint32_t)na;
+            phj ^= 1u;
           }
-          if (++a == (uint32_t)na) {
-            a = 0;
-            a_ph ^= 1u;
+          if (!mbar_wait(&aempty[aj], phj ^ 1u, abort_flag)) {
+            ok = false;
+            break;
           }
+          const uint8_t* wst = w_ring + s * p.w_stage_bytes + j * w_sub_bytes;
+          const uint8_t* tst = t_ring + s * p.t_stage_bytes;
+          uint32_t o[32];
+          dequant_half<FMT>(wst, row, half, tst, p.t_rows, p.axis, n, j, sub, o);
+          tmem_st32(tmem_a + lane_addr + aj * (uint32_t)kACols + (uint32_t)(half * 32), o);
+          if (p.norm_w) {
+            // chunk i of the sub-stage: 128-byte line i / 8 = (64-K block,
+            // token), 16-byte column (i % 8) XOR (line % 8) under the
+            // 128-byte swizzle (bn is a multiple of 16, so line % 8 is the
+            // token's); every chunk of a TMA stage lies inside [0, K)
+            uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
+            const float* wk =
+                reinterpret_cast<const float*>(t_ring + s * p.t_stage_bytes + p.nw_off) + j * kBK;
+            for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) {
+              const int line = i >> 3;                 // < 2 * bn
+              const bool hi = line >= p.bn;            // second 64-K block
+              const int t = hi ? line - p.bn : line;
+              const int kof = (hi ? 64 : 0) + (((i & 7) ^ (line & 7)) << 3);
+              if (p.x_bf16) norm_chunk<true>(xs + i, wk + kof, s_rinv[t]);
+              else norm_chunk<false>(xs + i, wk + kof, s_rinv[t]);
+            }
+            fence_proxy_async();
+          } else if (p.x_bf16) {
+            uint4* xs = reinterpret_cast<uint4*>(x_ring + s * x_stage_bytes + j * x_sub_bytes);
+            for (int i = pt; i < x_sub_bytes / 16; i += 128 * kHalves) bf16_to_f16_chunk(xs + i);
+            fence_proxy_async();
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[aj]);
         }
         if (!ok) break;
+        lsub += nsub;
+        a += (uint32_t)nsub;
+        while (a >= (uint32_t)na) {
+          a -= (uint32_t)na;
+          a_ph ^= 1u;
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);   // this warp is done with the stage
         if (++s == (uint32_t)ns) {
