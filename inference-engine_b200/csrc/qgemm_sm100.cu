@@ -297,6 +297,28 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+// Four 8-column loads (columns a, a + step, a + 2 step, a + 3 step of this
+// thread's lane) behind a single wait: one TMEM round trip instead of four.
+__device__ __forceinline__ void tmem_ld8x4(uint32_t a, uint32_t step, float (&v)[4][8]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%33];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%34];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%24,%25,%26,%27,%28,%29,%30,%31}, [%35];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(a), "r"(a + step), "r"(a + 2 * step), "r"(a + 3 * step)
+      : "memory");
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[q][i] = __uint_as_float(r[8 * q + i]);
+}
 // 32 consecutive TMEM columns of this thread's lane <- v[0..31]
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
@@ -1095,13 +1117,31 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       bool has_own = false;
       // this warp owns the 8-token column chunks c0 = 8 * (group + kGroups * i)
       for (int c0 = 8 * group; c0 < p.bn; c0 += 8 * kGroups) {
+        // accumulators summed in chain order 0, 1, ..., nacc - 1; four loads
+        // share one TMEM round trip when there are at least four
         float v[8];
-        tmem_ld8(tmem + lane_addr + (uint32_t)c0, v);
-        for (int c = 1; c < nacc; ++c) {
-          float w[8];
-          tmem_ld8(tmem + lane_addr + (uint32_t)(c * p.acc_cols + c0), w);
+        if (nacc % 4 == 0) {
+          {
+            float w[4][8];
+            tmem_ld8x4(tmem + lane_addr + (uint32_t)c0, (uint32_t)p.acc_cols, w);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] += w[j];
+            for (int j = 0; j < 8; ++j) v[j] = ((w[0][j] + w[1][j]) + w[2][j]) + w[3][j];
+          }
+          for (int c4 = 4; c4 < nacc; c4 += 4) {
+            float w[4][8];
+            tmem_ld8x4(tmem + lane_addr + (uint32_t)(c4 * p.acc_cols + c0), (uint32_t)p.acc_cols,
+                       w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = (((v[j] + w[0][j]) + w[1][j]) + w[2][j]) + w[3][j];
+          }
+        } else {
+          tmem_ld8(tmem + lane_addr + (uint32_t)c0, v);
+          for (int c = 1; c < nacc; ++c) {
+            float w[8];
+            tmem_ld8(tmem + lane_addr + (uint32_t)(c * p.acc_cols + c0), w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += w[j];
+          }
         }
         if constexpr (csplit) {
           if (crank > 0) {
