@@ -54,6 +54,11 @@ def parse():
     ap.add_argument("--scheme", default="int4-g128")
     ap.add_argument("--unfused-norm", action="store_true",
                     help="run each rms_norm as its own kernel instead of inside the next GEMM")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the isolated row-parallel GEMM + all-reduce sweep (one JSON line per "
+                         "case) instead of the decode step")
+    ap.add_argument("--sweep-m", default="1,8,64,512,4096,16384")
+    ap.add_argument("--sweep-formats", default="int8,int4-g128,fp8")
     return ap.parse_args()
 
 
@@ -371,13 +376,146 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# isolated fused row-parallel GEMM + all-reduce sweep
+# ---------------------------------------------------------------------------
+SWEEP_KN = ((14336, 4096), (28672, 8192))
+NVLINK_GBS = 770.0   # measured peer copy per direction on this pool's B200s
+
+
+def sweep_bounds(scheme: str, m: int, k: int, n: int, world: int, w_bytes: float,
+                 peaks: dict) -> dict:
+    """Lower bounds of one rank's fused launch: HBM bytes (packed weights, x,
+    out), tensor FLOPs and one-shot NVLink bytes ((world - 1) bf16 partials)."""
+    hbm = w_bytes + m * k * 2 + m * n * 2
+    flops = 2.0 * m * k * n
+    nvl = (world - 1) * m * n * 2
+    t = {"hbm": hbm / (peaks["hbm_gbs"] * 1e9),
+         "tensor": flops / (peaks["bf16_tflops"] * 1e12),
+         "nvlink": nvl / (NVLINK_GBS * 1e9)}
+    bound = max(t, key=t.get)
+    return {"bound": bound, "t_min_us": t[bound] * 1e6, "hbm_bytes": hbm, "flops": flops,
+            "nvlink_bytes": nvl}
+
+
+def run_sweep(args, rank: int, world: int, local: int) -> None:
+    """y = all_reduce(x_shard @ W_shard) for W [K, N] split by
+    K over the ranks, fused (qlinear with comm=) against the unfused build
+    (dequantize to bf16, cuBLAS GEMM, NCCL all-reduce), both timed with CUDA
+    events and taken as the max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    nccl = None
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        nccl = dist.new_group(backend="nccl")
+    from ie_tpq.comm import Communicator
+    from ie_tpq.linear import qlinear
+    from ie_tpq.packed import quantize_on_device
+
+    ms_list = [int(v) for v in args.sweep_m.split(",")]
+    formats = args.sweep_formats.split(",")
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        peaks = {"hbm_gbs": float(peaks["hbm_gbs"]), "bf16_tflops": float(peaks["bf16_tflops"])}
+        peak_src = "measured"
+    except (OSError, KeyError, ValueError):
+        peaks, peak_src = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+    max_bytes = max(ms_list) * max(n for _, n in SWEEP_KN) * 4
+    comm = Communicator(rank, world, max_bytes=max_bytes, timeout_s=10.0) if world > 1 else None
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, budget_ms: float = 60.0) -> float:
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        one = a.elapsed_time(b)
+        reps = int(max(3, min(50, budget_ms / max(one, 1e-3))))
+        reps = int(max_over_ranks(reps))   # every rank runs the same number of collectives
+        if world > 1:
+            dist.barrier()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b) / reps)
+
+    gen = torch.Generator(device="cuda")
+    for scheme in formats:
+        for kk, n in SWEEP_KN:
+            gen.manual_seed(0)
+            full = torch.randn((kk, n), generator=gen, device="cuda") * 0.02
+            k = kk // world
+            w = quantize_on_device(full, scheme).slice_k(rank * k, (rank + 1) * k)
+            del full
+            torch.cuda.empty_cache()
+            for m in ms_list:
+                gen.manual_seed(1 + rank)
+                x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+                out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+
+                def fused():
+                    qlinear(x, w, out=out, comm=comm)
+
+                def unfused():
+                    wd = w.dequantize("nk", torch.bfloat16)
+                    y = x @ wd.t()
+                    if world > 1:
+                        dist.all_reduce(y, group=nccl)
+
+                us_fused = timed(fused) * 1e3
+                us_unfused = timed(unfused) * 1e3
+                b = sweep_bounds(scheme, m, k, n, world, w.nbytes, peaks)
+                if rank == 0:
+                    print(json.dumps({
+                        "sweep": "fused row-parallel quant GEMM + all-reduce", "scheme": scheme,
+                        "K": kk, "N": n, "M": m, "tp": world, "k_per_rank": k,
+                        "us_fused": us_fused, "us_unfused": us_unfused,
+                        "speedup_vs_unfused": us_unfused / us_fused,
+                        "roofline": {"bound": b["bound"], "t_min_us": b["t_min_us"],
+                                     "frac": b["t_min_us"] / us_fused,
+                                     "peak_source": peak_src,
+                                     "nvlink_gbs": NVLINK_GBS},
+                        "hbm_bytes": b["hbm_bytes"], "flops": b["flops"],
+                        "nvlink_bytes": b["nvlink_bytes"]}), flush=True)
+                del x, out
+            del w
+            torch.cuda.empty_cache()
+    if comm is not None:
+        comm.check()
+        comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
     if world == 1 and args.gpus > 1:
         print(json.dumps({"error": "launch with torchrun for --gpus > 1"}))
         sys.exit(2)
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args, rank, world, local)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local)

@@ -1,0 +1,41 @@
+"""Host logic of bench.py's isolated sweep: which lower bound binds."""
+from __future__ import annotations
+
+import importlib.util
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+PEAKS = {"hbm_gbs": 6452.2, "bf16_tflops": 1661.6}
+
+
+@pytest.fixture(scope="module")
+def bench():
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def int4_bytes(k: int, n: int) -> float:
+    return k * n / 2 + (k // 128) * n * 4
+
+
+def test_decode_is_hbm_bound(bench):
+    b = bench.sweep_bounds("int4-g128", 1, 14336, 4096, 1, int4_bytes(14336, 4096), PEAKS)
+    assert b["bound"] == "hbm" and b["nvlink_bytes"] == 0
+    assert b["t_min_us"] == pytest.approx(b["hbm_bytes"] / (PEAKS["hbm_gbs"] * 1e3))
+
+
+def test_large_m_single_gpu_is_tensor_bound(bench):
+    b = bench.sweep_bounds("int8", 16384, 28672, 8192, 1, 28672 * 8192 + 4 * 28672, PEAKS)
+    assert b["bound"] == "tensor"
+    assert b["flops"] == 2.0 * 16384 * 28672 * 8192
+
+
+def test_large_m_at_tp8_is_nvlink_bound(bench):
+    k = 14336 // 8
+    b = bench.sweep_bounds("int4-g128", 4096, k, 4096, 8, int4_bytes(k, 4096), PEAKS)
+    assert b["bound"] == "nvlink"
+    assert b["nvlink_bytes"] == 7 * 4096 * 4096 * 2
