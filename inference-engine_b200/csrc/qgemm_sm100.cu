@@ -15,7 +15,7 @@
 //               accumulators in TMEM, 8 x K=16 per 128-K sub-stage;
 //               tcgen05.commit releases the stages.  With two issuers they take
 //               alternate sub-stages into separate accumulators.  For narrow
-//               token tiles the 8 MMAs of a sub-stage rotate over up to four
+//               token tiles the 8 MMAs of a sub-stage rotate over two
 //               accumulators, so consecutive MMAs do not wait on each other's
 //               results; the epilogue adds everything up.
 //   warps 3-18 dequantizers, then the epilogue.  They form four groups of four
@@ -1483,7 +1483,9 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   // pipe idle between its sub-stages (barrier wait, fence, commit), and shares
   // its scheduler with two dequant warps.
   pl.acc_cols = ((pl.bn + 15) / 16) * 16;
-  pl.chains = pl.bn <= 32 ? 4 : (pl.bn <= 64 ? 2 : 1);
+  // (Two chains for tiles up to 64 tokens: four were no faster in the mainloop
+  // and cost the epilogue a second TMEM round trip for the extra accumulators.)
+  pl.chains = pl.bn <= 64 ? 2 : 1;
   pl.issuers = (2 * pl.acc_cols * pl.chains + 4 * kACols <= 512) ? 2 : 1;
   const int accs = pl.acc_cols * pl.chains * pl.issuers;
   // The A ring covers a sub-stage's dequant plus its MMAs' latency (8 MMAs take
