@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (one process per GPU)
 
-Workload (the int4 Llama-3-8B-shaped decoder): one
+Workload (the headline config: the int4 Llama-3-8B-shaped decoder): one
 decode step of the whole model's quantized linear path -- 32 layers x
 {rms_norm + qkv (column; the norm folded into the GEMM), o (row + fused
 all-reduce + residual), rms_norm + gate/up (column, folded norm, fused
@@ -399,7 +399,7 @@ def sweep_bounds(scheme: str, m: int, k: int, n: int, world: int, w_bytes: float
 
 
 def run_sweep(args, rank: int, world: int, local: int) -> None:
-    """y = all_reduce(x_shard @ W_shard) for W [K, N] split by
+    """The isolated row-parallel sweep: y = all_reduce(x_shard @ W_shard) for W [K, N] split by
     K over the ranks, fused (qlinear with comm=) against the unfused build
     (dequantize to bf16, cuBLAS GEMM, NCCL all-reduce), both timed with CUDA
     events and taken as the max over ranks."""
