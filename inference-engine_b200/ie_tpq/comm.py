@@ -19,6 +19,19 @@ from . import _lib
 from .device import dtype_code, require_cuda
 
 
+def gather_in_rank_order(own: bytes, world_size: int, group=None) -> bytes:
+    """Every rank's ``own`` bytes, concatenated in rank order, through the
+    process group (host objects only, so any backend works: gloo on CPU,
+    NCCL or gloo beside the GPUs).  All ranks must pass blobs of one length."""
+    import torch.distributed as dist
+
+    parts = [None] * world_size
+    dist.all_gather_object(parts, own, group=group)
+    if any(not isinstance(p, bytes) or len(p) != len(own) for p in parts):
+        raise ValueError("every rank must contribute a handle of the same length")
+    return b"".join(parts)
+
+
 class Communicator:
     def __init__(self, rank: int, world_size: int, device=None, max_bytes: int = 64 << 20,
                  group=None, timeout_s: float = 2.0, _loopback: bool = False):
@@ -40,13 +53,10 @@ class Communicator:
         _lib.check(_lib.lib().ie_comm_export(self._h, mine), "comm_export")
         own = mine.raw
         if _loopback or world_size == 1:
-            handles = [own] * world_size
+            joined = own * world_size
         else:
-            import torch.distributed as dist
-
-            handles = [None] * world_size
-            dist.all_gather_object(handles, own, group=group)
-        blob = ctypes.create_string_buffer(b"".join(handles), len(handles) * len(own))
+            joined = gather_in_rank_order(own, world_size, group)
+        blob = ctypes.create_string_buffer(joined, world_size * len(own))
         _lib.check(_lib.lib().ie_comm_open(self._h, blob), "comm_open")
         self.set_timeout(timeout_s)
         if not _loopback and world_size > 1:
