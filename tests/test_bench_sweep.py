@@ -1,4 +1,4 @@
-"""Host logic of bench.py's isolated sweep: which lower bound binds."""
+"""Host logic of bench.py: the isolated sweep's lower bounds and the traffic field."""
 from __future__ import annotations
 
 import importlib.util
@@ -39,3 +39,22 @@ def test_large_m_at_tp8_is_nvlink_bound(bench):
     b = bench.sweep_bounds("int4-g128", 4096, k, 4096, 8, int4_bytes(k, 4096), PEAKS)
     assert b["bound"] == "nvlink"
     assert b["nvlink_bytes"] == 7 * 4096 * 4096 * 2
+
+
+def test_traffic_field_comes_from_the_committed_capture(bench):
+    """The bench line's roofline.traffic is the gate/up DRAM bytes of the
+    committed ncu summary, scaled to a rank's launch by algorithmic bytes."""
+    from types import SimpleNamespace
+
+    shape = SimpleNamespace(hidden=4096, intermediate=14336)
+    args = SimpleNamespace(scheme="int4-g128", batch=16)
+    h, i = shape.hidden, shape.intermediate
+    tp1 = (h * 2 * i / 2 + (h // 128) * 2 * i * 4) + 16 * h * 2 + 16 * i * 2
+    traffic, src = bench.measured_traffic(args, tp1, shape)
+    assert src.endswith("qgemm_tc_int4g128_b16_ncu_full.md")
+    # within 1 % of the algorithmic bytes: nothing is fetched twice
+    assert abs(traffic - tp1) / tp1 < 0.01
+    half, _ = bench.measured_traffic(args, tp1 / 2, shape)
+    assert half == pytest.approx(traffic / 2)
+    other, why = bench.measured_traffic(SimpleNamespace(scheme="int8", batch=16), tp1, shape)
+    assert other is None and "no capture" in why
