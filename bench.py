@@ -15,13 +15,25 @@ fixed: strong scaling).  Attention is outside the path (see ie_tpq.stack).
 ``value`` = tokens/s of the step with inputs resident in HBM (CUDA-graph
 replay timed with CUDA events, max over ranks).  ``e2e`` = the same through
 host buffers: pinned H2D copy of the step's input, the step, D2H copy of its
-output, every step.  The weights (3.5 GB at TP=1, 0.44 GB per rank at TP=8)
+output, every step.  The weights (3.7 GB at TP=1, 0.46 GB per rank at TP=8)
 exceed the 126 MB L2, so no flush is needed between steps.
+
+Also in the line, all measured in the same run:
+  * ``parity`` -- one eager pass of a layer at the bench's own shard shapes,
+    every projection's output compared with the CPU oracle (rtol 2e-2 / atol
+    2e-3) on a seeded subset of output columns, and the reduced outputs of all
+    ranks compared bitwise;
+  * ``dense_cublas`` -- the same step built the way the reference's GPU model
+    runs it (ie/model/torch_transformer.py:15-29,36-38,60): dense bf16 weights
+    resident on the device, torch matmul (cuBLAS), unfused norm / SiLU /
+    residual, and an NCCL all-reduce per row-parallel layer at N > 1;
+  * ``decode_batches`` -- the step at decode batches 1, 16, 64 and 256;
+  * ``cpu_baseline`` -- the reference's NumPy path on the host cores.
 
 ``--impl reference`` times the reference's CPU path (the NumPy restatement in
 oracle/, f32 dequantized weights, ranks run one after another as in
 ie/parallel/tensor_parallel.py:65-73) on rank 0 with all host threads, on a
-bounded sample of the same workload, scaled to the full step.
+bounded sample of the same workload (whole layers), scaled to the full step.
 """
 from __future__ import annotations
 
@@ -41,6 +53,7 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "quant TP linear+allreduce % roofline; decode tok/s at TP=1/2/4/8"
 UNIT = "tok/s"
+RTOL, ATOL = 2e-2, 2e-3
 
 
 def parse():
@@ -54,6 +67,12 @@ def parse():
     ap.add_argument("--scheme", default="int4-g128")
     ap.add_argument("--unfused-norm", action="store_true",
                     help="run each rms_norm as its own kernel instead of inside the next GEMM")
+    ap.add_argument("--batches", default="1,16,64,256",
+                    help="decode batches also timed (the decode_batches field); empty to skip")
+    ap.add_argument("--no-dense", action="store_true", help="skip the dense cuBLAS comparator")
+    ap.add_argument("--no-parity", action="store_true", help="skip the in-run parity check")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="wall-clock budget of the CPU baseline sample")
     ap.add_argument("--sweep", action="store_true",
                     help="the isolated row-parallel GEMM + all-reduce sweep (one JSON line per "
                          "case) instead of the decode step")
@@ -124,8 +143,15 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # the reference's CPU path (oracle port), bounded sample
 # ---------------------------------------------------------------------------
-def cpu_reference(args, world: int) -> dict:
+def cpu_reference(args, world: int, steps: int | None = None, warmup: int = 1) -> dict:
+    """The reference's NumPy path for this workload on every host core: whole
+    layers of ie/parallel/tensor_parallel.py:65-73 (ranks one after another),
+    f32 dequantized weights.  One timed unit is one layer (a bounded sample of
+    the step); ``steps`` units are timed after ``warmup`` (or, with steps None,
+    as many as fit in ``--cpu-seconds``) and scaled to the full step.
+    torchrun pins OMP_NUM_THREADS=1, so the BLAS pool is widened explicitly."""
     import numpy as np
+    from threadpoolctl import threadpool_info, threadpool_limits
 
     from oracle import tpq_oracle as o
 
@@ -158,33 +184,46 @@ def cpu_reference(args, world: int) -> dict:
         parts = [o.sharded_mlp_partial(x, norm, wg, wu, wd, r, world) for r in range(world)]
         return x + o.all_reduce(parts)
 
-    layer(x)
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        layer(x)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el > 10.0 or reps >= 50:
-            break
+    with threadpool_limits(limits=cores, user_api="blas"):
+        threads = max((p.get("num_threads", 1) for p in threadpool_info()
+                       if p.get("user_api") == "blas"), default=1)
+        for _ in range(max(1, warmup)):
+            layer(x)
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            layer(x)
+            reps += 1
+            el = time.perf_counter() - t0
+            if steps is not None:
+                if reps >= steps:
+                    break
+            elif el > args.cpu_seconds or reps >= 200:
+                break
     per_layer = el / reps
     step = per_layer * args.layers
-    return {"value": args.batch / step, "unit": UNIT, "cores": cores, "kind": "port",
+    return {"value": args.batch / step, "unit": UNIT, "cores": cores, "threads": threads,
+            "kind": "port", "layers_timed": reps, "extrapolated_from_layers": 1,
             "sample": (f"{reps} passes over 1 of {args.layers} layers (Llama-3-8B shapes, "
                        f"batch {args.batch}, TP={world} ranks in sequence), NumPy f32 on "
-                       f"dequantized weights, scaled x{args.layers}"),
-            "ms_per_step": step * 1e3}
+                       f"dequantized weights with {threads} BLAS threads on {cores} cores, "
+                       f"scaled x{args.layers} to the step"),
+            "ms_per_step": step * 1e3, "ms_timed": el * 1e3}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    base = cpu_reference(args, world)
+    base = cpu_reference(args, world, steps=args.steps, warmup=args.warmup)
     cfg = workload_config(args, world)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "steps_note": (f"each step is a bounded sample of the decode step: one whole layer "
+                           f"of the {args.layers}; the time per layer is scaled to the step"),
             "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "threads", "kind",
+                                                  "sample", "extrapolated_from_layers",
+                                                  "layers_timed")},
             "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -227,18 +266,221 @@ def workload_config(args, world: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# in-run parity at the bench's shard shapes
+# ---------------------------------------------------------------------------
+PARITY_COLS = 384
+
+
+def parity_check(args, rank: int, world: int, shape, layer, seed: int, dist) -> dict:
+    """One eager pass of a layer at this run's shard shapes, each projection
+    compared with the CPU oracle on the GPU's own inputs to that projection.
+
+    The oracle needs the f32 weights: rank 0 regenerates the layer's full
+    weights with the seed ``synthetic_layer`` used and quantizes a seeded
+    subset of PARITY_COLS output columns of each projection with the oracle's
+    group-128 quantizer (group tables are per output column, so a column
+    subset quantizes exactly as in the whole weight).  The reduced outputs of
+    the row-parallel projections are compared bitwise across ranks."""
+    import numpy as np
+    import torch
+
+    from ie_tpq.linear import qlinear
+    from ie_tpq.tensor_parallel import rms_norm
+    from oracle import tpq_oracle as o
+
+    h, inter = shape.hidden, shape.intermediate
+    q_cols = shape.q_out // world
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4242)
+    x = torch.randn((args.batch, h), generator=gen, device="cuda").to(torch.bfloat16)
+    norm = torch.ones(h, dtype=torch.float32, device="cuda")
+    comm = layer.get("_comm")
+    if "qkv" in layer:
+        qkv = qlinear(x, layer["qkv"], norm_weight=norm)
+    else:
+        qkv = torch.cat([qlinear(x, layer[n], norm_weight=norm) for n in ("q", "k", "v")], 1)
+    a = qkv[:, :q_cols].contiguous()
+    x1 = qlinear(a, layer["o"], residual=x, comm=comm if world > 1 else None)
+    u = qlinear(x1, layer["gate_up"], norm_weight=norm)
+    x2 = qlinear(u, layer["down"], residual=x1, comm=comm if world > 1 else None)
+    torch.cuda.synchronize()
+    host = {k: v.float().cpu().numpy() for k, v in
+            (("x", x), ("qkv", qkv), ("a", a), ("x1", x1), ("u", u), ("x2", x2))}
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, host)
+    else:
+        gathered = [host]
+    if rank != 0:
+        return {}
+    bitwise = all(np.array_equal(g["x1"], gathered[0]["x1"]) and
+                  np.array_equal(g["x2"], gathered[0]["x2"]) for g in gathered)
+    # the layer's full f32 weights, in the order synthetic_layer draws them
+    full = {}
+    g2 = torch.Generator(device="cuda")
+    g2.manual_seed(seed)
+    for name, (k, n) in (("q", (h, shape.q_out)), ("k", (h, shape.kv_out)),
+                         ("v", (h, shape.kv_out)), ("o", (shape.q_out, h)),
+                         ("gate", (h, inter)), ("up", (h, inter)), ("down", (inter, h))):
+        full[name] = torch.randn((k, n), generator=g2, device="cuda", dtype=torch.float32) * 0.02
+    rng = np.random.default_rng(99)
+
+    def deq_cols(w, cols):
+        sub = w[:, torch.as_tensor(cols, device="cuda")].cpu().numpy()
+        if args.scheme == "int4-g128":
+            return o.quantize_int4_group128(sub).dequantized()
+        raise ValueError("parity check implemented for int4-g128")
+
+    report, ok, worst = {}, bitwise, 0.0
+
+    def compare(name, got, want):
+        nonlocal ok, worst
+        err = np.abs(got - want)
+        fine = bool(np.all(err <= ATOL + RTOL * np.abs(want)))
+        ok = ok and fine
+        worst = max(worst, float(err.max()))
+        report[name] = {"ok": fine, "max_abs": float(err.max()), "cols": int(got.shape[1])}
+
+    heads = shape.heads
+    hd = shape.head_dim
+    xs = gathered[0]["x"]
+    n0 = o.rms_norm(xs, np.ones(h, np.float32))
+    # qkv: rank r holds heads [r H/w, (r+1) H/w) of q, k and v
+    q_all = np.concatenate([g["qkv"][:, :q_cols] for g in gathered], axis=1)
+    cols = np.sort(rng.choice(shape.q_out, size=min(PARITY_COLS, shape.q_out), replace=False))
+    compare("qkv(q heads)", q_all[:, cols], n0 @ deq_cols(full["q"], cols))
+    # o: x1 = x + sum_r a_r @ Wo[rows of r]
+    a_all = np.concatenate([g["a"] for g in gathered], axis=1)
+    cols = np.sort(rng.choice(h, size=PARITY_COLS, replace=False))
+    compare("o+allreduce+residual", gathered[0]["x1"][:, cols],
+            xs[:, cols] + a_all @ deq_cols(full["o"], cols))
+    # gate/up: rank r holds columns [r I/w, (r+1) I/w) of both
+    n1 = o.rms_norm(gathered[0]["x1"], np.ones(h, np.float32))
+    u_all = np.concatenate([g["u"] for g in gathered], axis=1)
+    cols = np.sort(rng.choice(inter, size=PARITY_COLS, replace=False))
+    want = o.silu(n1 @ deq_cols(full["gate"], cols)) * (n1 @ deq_cols(full["up"], cols))
+    compare("gate/up+silu", u_all[:, cols], want)
+    cols = np.sort(rng.choice(h, size=PARITY_COLS, replace=False))
+    compare("down+allreduce+residual", gathered[0]["x2"][:, cols],
+            gathered[0]["x1"][:, cols] + u_all @ deq_cols(full["down"], cols))
+    del full
+    torch.cuda.empty_cache()
+    return {"ok": ok, "max_abs": worst, "ranks_bitwise_equal": bitwise, "rtol": RTOL,
+            "atol": ATOL, "oracle": "oracle/tpq_oracle.py int4 group-128, f32 dequant-matmul",
+            "shapes": {"qkv": [h, (shape.q_out + 2 * shape.kv_out) // world],
+                       "o": [shape.q_out // world, h], "gate_up": [h, 2 * inter // world],
+                       "down": [inter // world, h]},
+            "tokens": args.batch, "projections": report}
+
+
+# ---------------------------------------------------------------------------
+# the comparator: dense bf16 weights, cuBLAS, NCCL (the reference's GPU model)
+# ---------------------------------------------------------------------------
+def dense_step(args, world: int, shape, steps: int, warmup: int, nccl, max_over_ranks, barrier):
+    """The decode step's linear path as TorchTransformer runs it: dense bf16
+    weights resident on the device, ``x @ W`` on cuBLAS for every projection,
+    rms_norm / SiLU*up / residual as separate torch ops, and an NCCL all-reduce
+    after each row-parallel projection at N > 1.  Weight values do not change
+    cuBLAS time, so they are random bf16 drawn on the device.  Returns ms per
+    step (CUDA-graph replay, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    h, inter = shape.hidden, shape.intermediate
+    qkv_n = (shape.q_out + 2 * shape.kv_out) // world
+    q_cols = shape.q_out // world
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    mk = lambda n, k: (torch.randn((n, k), generator=gen, device="cuda",
+                                   dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    layers = [{"qkv": mk(qkv_n, h), "o": mk(h, q_cols), "gu": mk(2 * inter // world, h),
+               "down": mk(h, inter // world)} for _ in range(args.layers)]
+    norm = torch.ones(h, dtype=torch.bfloat16, device="cuda")
+    x_in = torch.randn((args.batch, h), generator=gen, device="cuda").to(torch.bfloat16)
+    x_out = torch.empty_like(x_in)
+    half = inter // world
+
+    def step():
+        x = x_in
+        for L in layers:
+            n = F.rms_norm(x, (h,), norm, 1e-6)
+            qkv = n @ L["qkv"].t()
+            o_ = qkv[:, :q_cols] @ L["o"].t()
+            if world > 1:
+                dist.all_reduce(o_, group=nccl)
+            x = x + o_
+            n = F.rms_norm(x, (h,), norm, 1e-6)
+            gu = n @ L["gu"].t()
+            u = F.silu(gu[:, :half]) * gu[:, half:]
+            d = u @ L["down"].t()
+            if world > 1:
+                dist.all_reduce(d, group=nccl)
+            x = x + d
+        x_out.copy_(x)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b) / steps)
+    wbytes = sum(t.numel() * 2 for L in layers for t in L.values())
+    del g, layers
+    torch.cuda.empty_cache()
+    return ms, wbytes
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def timed_replays(fn, steps: int, warmup: int, barrier, max_over_ranks):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    return max_over_ranks(a.elapsed_time(b) / steps)
+
+
 def run_ours(args, rank: int, world: int, local: int) -> None:
     import torch
 
     torch.cuda.set_device(local)
     import torch.distributed as dist
 
+    nccl = None
     if world > 1:
         import datetime
 
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
+        if not args.no_dense:
+            nccl = dist.new_group(backend="nccl")
     from ie_tpq.comm import Communicator
     from ie_tpq.linear import qlinear
     from ie_tpq.sharding import Shard
@@ -248,8 +490,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     shard = Shard(rank, world)
     comm = None
     if world > 1:
-        comm = Communicator(rank, world, max_bytes=max(args.batch * shape.hidden * 4, 1 << 20),
-                            timeout_s=10.0)
+        comm = Communicator(rank, world, max_bytes=max(max(args.batch, 256) * shape.hidden * 4,
+                                                       1 << 20), timeout_s=10.0)
     layers = [synthetic_layer(shape, args.scheme, shard, seed=1000 + li)
               for li in range(args.layers)]
     stack = LinearStack(shape, layers, args.batch, torch.bfloat16, comm=comm, world=world,
@@ -258,6 +500,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     gen.manual_seed(7)
     stack.x_in.copy_(torch.randn(stack.x_in.shape, generator=gen, device="cuda"))
     stack.capture()
+    launches_per_step = stack.launches_per_step   # this library's kernels per step
 
     def barrier():
         if world > 1:
@@ -299,19 +542,26 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     x_host = torch.empty(stack.x_in.shape, dtype=stack.dtype).pin_memory()
     x_host.copy_(stack.x_in.cpu())
     out_host = torch.empty(stack.x_out.shape, dtype=stack.dtype).pin_memory()
-    for _ in range(args.warmup):
-        stack.run_host(x_host, out_host)
-    torch.cuda.synchronize()
-    barrier()
-    start.record()
-    for _ in range(args.steps):
-        stack.run_host(x_host, out_host)
-    end.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    e2e_ms = timed_replays(lambda: stack.run_host(x_host, out_host), args.steps, args.warmup,
+                           barrier, max_over_ranks)
     if comm is not None:
         comm.check()
+
+    # ---- the step at other decode batches ----------------------------------
+    batches = {}
+    for b in [int(v) for v in args.batches.split(",") if v.strip()]:
+        if b == args.batch:
+            batches[str(b)] = {"tok_s": value, "ms_per_step": ms}
+            continue
+        st = LinearStack(shape, layers, b, torch.bfloat16, comm=comm, world=world,
+                         fuse_norm=not args.unfused_norm)
+        st.x_in.copy_(torch.randn(st.x_in.shape, generator=gen, device="cuda"))
+        st.capture()
+        reps = max(20, min(args.steps, 200))
+        bms = timed_replays(st.replay, reps, 3, barrier, max_over_ranks)
+        batches[str(b)] = {"tok_s": b / (bms / 1e3), "ms_per_step": bms, "steps": reps}
+        del st
+    torch.cuda.empty_cache()
 
     # ---- dominant kernel: the gate/up launch of every layer, graph-replayed --
     wb = layer_weight_bytes(shape, args.scheme, world)
@@ -338,12 +588,36 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     kern_bytes = wb["gate_up"] + args.batch * shape.hidden * 2 + args.batch * (inter // 2) * 2
     achieved = kern_bytes / (kern_ms / 1e3) / 1e9
     traffic, traffic_src = measured_traffic(args, kern_bytes, shape)
-    peaks = {}
     try:
         peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
         peak, peak_src = float(peaks["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         peak, peak_src = 6650.0, "fallback"
+    del kg, outs
+    torch.cuda.empty_cache()
+
+    # ---- parity of one layer at these shard shapes ---------------------------
+    parity = None
+    if not args.no_parity:
+        layer0 = dict(layers[0])
+        layer0["_comm"] = comm
+        parity = parity_check(args, rank, world, shape, layer0, 1000, dist)
+
+    # ---- the dense cuBLAS (+ NCCL) comparator --------------------------------
+    dense = None
+    weight_bytes = args.layers * sum(wb.values())
+    if not args.no_dense:
+        del stack
+        layers.clear()
+        torch.cuda.empty_cache()
+        dms, dbytes = dense_step(args, world, shape, max(20, min(args.steps, 300)), 5, nccl,
+                                 max_over_ranks, barrier)
+        dense = {"value": args.batch / (dms / 1e3), "unit": UNIT, "ms_per_step": dms,
+                 "speedup_of_ours": value / (args.batch / (dms / 1e3)),
+                 "weights_bytes_per_rank": dbytes,
+                 "what": ("dense bf16 weights resident, torch matmul (cuBLAS), unfused "
+                          "rms_norm/SiLU/residual" + (", NCCL all-reduce" if world > 1 else "") +
+                          "; CUDA graph, CUDA events, max over ranks")}
 
     if rank == 0:
         base = cpu_reference(args, world)
@@ -358,29 +632,38 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                          "kernel": "qgemm_tc_kernel (tcgen05) gate/up, int4-g128, fused SiLU*up",
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
                          "algorithmic_bytes_per_launch": kern_bytes,
-                         "launch_us": kern_ms * 1e3},
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                         "launch_us": kern_ms * 1e3,
+                         "step_weight_bytes_per_rank": weight_bytes,
+                         "step_frac": weight_bytes / (ms / 1e3) / 1e9 / peak},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "threads", "kind",
+                                                  "sample", "extrapolated_from_layers",
+                                                  "layers_timed")},
             "e2e": {"value": args.batch / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
-            "gpu_launches": stack.launches_per_step * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
-            "weights_bytes_per_rank": args.layers * sum(wb.values()),
+            "parity": parity,
+            "dense_cublas": dense,
+            "decode_batches": batches,
+            "weights_bytes_per_rank": weight_bytes,
         }
         print(json.dumps(line), flush=True)
     barrier()
-    del stack
     if comm is not None:
         comm.close()
     if world > 1:
+        if nccl is not None:
+            dist.destroy_process_group(nccl)
         dist.destroy_process_group()
+
 
 
 # ---------------------------------------------------------------------------
 # isolated fused row-parallel GEMM + all-reduce sweep
 # ---------------------------------------------------------------------------
 SWEEP_KN = ((14336, 4096), (28672, 8192))
-NVLINK_GBS = 770.0   # measured peer copy per direction on this pool's B200s
+NVLINK_GBS = 770.0   # measured B200 peer copy bandwidth, GB/s per direction
 
 
 def sweep_bounds(scheme: str, m: int, k: int, n: int, world: int, w_bytes: float,
@@ -400,9 +683,12 @@ def sweep_bounds(scheme: str, m: int, k: int, n: int, world: int, w_bytes: float
 
 def run_sweep(args, rank: int, world: int, local: int) -> None:
     """The isolated row-parallel sweep: y = all_reduce(x_shard @ W_shard) for W [K, N] split by
-    K over the ranks, fused (qlinear with comm=) against the unfused build
-    (dequantize to bf16, cuBLAS GEMM, NCCL all-reduce), both timed with CUDA
-    events and taken as the max over ranks."""
+    K over the ranks, fused (qlinear with comm=) against two unfused builds,
+    all timed with CUDA events and taken as the max over ranks:
+      * ``us_unfused`` -- dequantize the shard to bf16 on every call, cuBLAS GEMM,
+        NCCL all-reduce (a quantized model served without a fused kernel);
+      * ``us_dense`` -- the dequantized bf16 shard kept resident (the reference's
+        own GPU model, ie/model/torch_transformer.py:15-29), cuBLAS GEMM, NCCL."""
     import datetime
 
     import torch
@@ -466,6 +752,8 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
             k = kk // world
             w = quantize_on_device(full, scheme).slice_k(rank * k, (rank + 1) * k)
             del full
+            # the dense comparator keeps the dequantized bf16 shard resident
+            w_dense = w.dequantize("nk", torch.bfloat16)
             torch.cuda.empty_cache()
             for m in ms_list:
                 gen.manual_seed(1 + rank)
@@ -481,15 +769,22 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
                     if world > 1:
                         dist.all_reduce(y, group=nccl)
 
+                def dense():
+                    y = x @ w_dense.t()
+                    if world > 1:
+                        dist.all_reduce(y, group=nccl)
+
                 us_fused = timed(fused) * 1e3
                 us_unfused = timed(unfused) * 1e3
+                us_dense = timed(dense) * 1e3
                 b = sweep_bounds(scheme, m, k, n, world, w.nbytes, peaks)
                 if rank == 0:
                     print(json.dumps({
                         "sweep": "fused row-parallel quant GEMM + all-reduce", "scheme": scheme,
                         "K": kk, "N": n, "M": m, "tp": world, "k_per_rank": k,
-                        "us_fused": us_fused, "us_unfused": us_unfused,
+                        "us_fused": us_fused, "us_unfused": us_unfused, "us_dense": us_dense,
                         "speedup_vs_unfused": us_unfused / us_fused,
+                        "speedup_vs_dense": us_dense / us_fused,
                         "roofline": {"bound": b["bound"], "t_min_us": b["t_min_us"],
                                      "frac": b["t_min_us"] / us_fused,
                                      "peak_source": peak_src,
@@ -497,7 +792,7 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
                         "hbm_bytes": b["hbm_bytes"], "flops": b["flops"],
                         "nvlink_bytes": b["nvlink_bytes"]}), flush=True)
                 del x, out
-            del w
+            del w, w_dense
             torch.cuda.empty_cache()
     if comm is not None:
         comm.check()

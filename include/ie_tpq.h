@@ -155,15 +155,17 @@ int ie_dequantize(const ie_qweight* w, int32_t layout, int32_t out_dtype, void* 
  * (ie/kernels/torch_backend.py:125-127) on a packed shard. */
 /* Bytes of caller-owned workspace the call would use (split-K partials and
  * tile tickets of the tensor-core kernel); the first 256-byte-rounded region
- * holds tickets that must be zero before first use and are left zero. */
+ * holds the tickets, which the call clears on the stream before the kernel
+ * runs (so a launch that gave up on an expired wait leaves nothing behind). */
 size_t ie_qlinear_workspace_size(const ie_qlinear_args* a);
 int ie_qlinear(const ie_qlinear_args* a, void* stream);
 
 /* ---- quantized linear that allocates nothing ----------------------------------
  * No counterpart in the reference (whose linear layers are CPU numpy): an
- * addition for callers that cannot allocate device memory at call time -- work
- * recorded into a CUDA graph with a fixed memory plan, or an engine whose
- * allocator owns all of HBM -- yet want the split-K tensor-core kernel.
+ * addition for callers that cannot allocate device memory at call time -- an
+ * engine whose allocator has already claimed all the HBM it may use, or a
+ * latency-bound decode loop that must never enter the CUDA allocator -- yet
+ * want the split-K tensor-core kernel.
  * Same arguments and result as ie_qlinear on the tensor-core path; workspace
  * and workspace_bytes are ignored.  The split-K partials and tile tickets live
  * in a static device array of IE_QLINEAR_NOALLOC_SCRATCH_BYTES inside the

@@ -3,7 +3,7 @@
 //
 // The weight is the MMA's A operand (M = 128 output rows per tile) and the
 // token batch is its N dimension (16..256), so decode batches and prefill
-// batches use the same kernel.  Per CTA (352 threads, one CTA per SM):
+// batches use the same kernel.  Per CTA (608 threads = 19 warps, one CTA per SM):
 //
 //   warp 0      TMA producer: the packed weight tile [128 rows x 128 K]
 //               (64- or 128-byte swizzle), the activation tile [BN tokens x
@@ -377,6 +377,15 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cas
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return h2_bits(__floats2half2_rn(a, b));
 }
+// f32 pair -> f16x2 (a in the low half), saturating: magnitudes beyond f16's
+// largest finite value (65504) become +-65504 instead of +-inf.  Activations
+// reach the tensor cores as f16, so a bf16 activation outside f16's range is
+// clamped to it; one instruction, the same cost as the plain conversion.
+__device__ __forceinline__ uint32_t pack_h2_sat(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
 
 // ---------------------------------------------------------------------------
 // dequantization of 32 K values of one row into 16 f16x2 words (TMEM columns)
@@ -572,13 +581,13 @@ __device__ __forceinline__ void store8(void* out, int dt, int64_t base, int64_t 
   }
 }
 
-// bf16 -> f16 of one 16-byte chunk (8 values), in place.
+// bf16 -> f16 of one 16-byte chunk (8 values), in place, saturating at +-65504.
 __device__ __forceinline__ void bf16_to_f16_chunk(uint4* p) {
   uint4 v = *p;
   uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    w[i] = pack_h2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+    w[i] = pack_h2_sat(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
   *p = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -596,7 +605,7 @@ __device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
 __device__ __forceinline__ uint32_t f32x2_to_h2(uint64_t v) {
   float lo, hi;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return pack_h2(lo, hi);
+  return pack_h2_sat(lo, hi);
 }
 
 // RMS-norm prologue, one 16-byte chunk of the x tile (8 consecutive K of one
@@ -1394,15 +1403,25 @@ struct Plan {
   int recv_bytes = 0;
 };
 
+// Per-device caches are indexed by the current device's ordinal, so a process
+// that drives GPUs of different sizes plans each launch for its own device.
+constexpr int kMaxDevOrdinals = 64;
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return (dev >= 0 && dev < kMaxDevOrdinals) ? dev : 0;
+}
+
 int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+  static int n[kMaxDevOrdinals] = {};
+  const int dev = current_device();
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
   }
-  return n;
+  return n[dev];
 }
 
 int fmt_of(const ie_qweight& w) {
@@ -1560,18 +1579,26 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3((unsigned)(tiles * pl.splits));
+  // occupancy of one (shared memory, cluster size) configuration, per device
   static std::mutex mu;
-  static int cached_key[4] = {-1, -1, -1, -1}, cached_max[4] = {0, 0, 0, 0};
+  static int cached_key[kMaxDevOrdinals][4], cached_max[kMaxDevOrdinals][4];
+  static bool cache_init = false;
   int max_clusters = 0;
   {
     std::lock_guard<std::mutex> lock(mu);
+    if (!cache_init) {
+      for (auto& row : cached_key)
+        for (int& k : row) k = -1;
+      cache_init = true;
+    }
+    const int dev = current_device();
     const int key = (int)pl.smem * 16 + pl.splits;
-    if (cached_key[FMT] == key) {
-      max_clusters = cached_max[FMT];
+    if (cached_key[dev][FMT] == key) {
+      max_clusters = cached_max[dev][FMT];
     } else {
       IE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, (const void*)kern, &cfg));
-      cached_key[FMT] = key;
-      cached_max[FMT] = max_clusters;
+      cached_key[dev][FMT] = key;
+      cached_max[dev][FMT] = max_clusters;
     }
   }
   if (max_clusters <= 0)
@@ -1708,6 +1735,12 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   if (pl.splits > 1 && !pl.csplit) {
     prm.counters = static_cast<uint32_t*>(a.workspace);
     prm.ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pl.counters_bytes);
+    // The finalizing CTA of a tile resets its ticket, but a launch that gave up
+    // on an expired wait leaves the tickets of its unfinished tiles counted; a
+    // later launch on the same workspace would then finalize a tile before all
+    // of its splits arrived.  Clearing them first makes every launch start
+    // from zero whatever happened before.
+    IE_CUDA_TRY(cudaMemsetAsync(a.workspace, 0, pl.counters_bytes, s));
   }
   prm.x_bf16 = a.act_dtype == IE_DT_BF16 ? 1 : 0;
   if (a.epilogue & IE_EPI_RMS_NORM) {
@@ -1727,9 +1760,10 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
 
 // ---------------------------------------------------------------------------
 // Static split-K scratch (ie_qlinear_noalloc).  Callers that may not allocate
-// device memory -- code recorded into a CUDA graph whose memory plan is fixed,
-// an engine whose allocator owns every byte of HBM, a real-time decode loop --
-// still need somewhere for the f32 split-K partials and tile tickets.  This
+// device memory at call time -- an engine whose allocator has already claimed
+// every byte of HBM it may use, or a real-time decode loop that must never
+// enter the CUDA allocator -- still need somewhere for the f32 split-K
+// partials and tile tickets.  This
 // array is part of the module image: the driver reserves it on each device
 // when the module loads, so using it never allocates.  It is shared by every
 // call on a device: two such calls overlapping on the GPU (different streams,
@@ -1786,9 +1820,8 @@ int launch_qlinear_tc_static(const ie_qlinear_args& a, cudaStream_t s) {
   ie_qlinear_args b = a;
   b.workspace = scratch;
   b.workspace_bytes = IE_QLINEAR_NOALLOC_SCRATCH_BYTES;
-  // tickets must read zero when the kernel starts; a call that ended early on an
-  // expired wait may have left some set
-  if (pl.splits > 1) IE_CUDA_TRY(cudaMemsetAsync(scratch, 0, pl.counters_bytes, s));
+  // launch_qlinear_tc clears the tile tickets at the start of the array before
+  // a split-K launch, so they read zero even after a call that ended early
   return launch_qlinear_tc(b, nullptr, s);
 }
 

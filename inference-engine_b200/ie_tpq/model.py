@@ -1,0 +1,208 @@
+"""A decoder whose linear layers are this library's quantized tensor-parallel
+shards, behind the reference engine's model protocol.
+
+``QuantizedTransformer`` implements what ``Engine`` calls on a model
+(ie/engine/engine.py:38-95, as ``TorchTransformer`` does in
+ie/model/torch_transformer.py:82-140): ``allocate_caches``, ``uses_flash``,
+``run``, ``forward``, ``logits_for_last_token_of_each``, ``logits_on_device``,
+``sample``, plus ``config``, ``device``, ``dtype`` and ``graphs`` (so the
+reference's ``DecodeGraphs`` can capture and replay its decode step).
+
+One instance holds ONE tensor-parallel rank (``shard``); with one process per
+GPU every rank builds its own instance from the same source model and steps the
+same schedule, and the row-parallel o / down projections reduce across ranks
+inside their GEMM epilogues through ``comm`` (ie/parallel/tensor_parallel.py:59-73
+restated as SPMD).  Per layer (TorchBlock.forward, torch_transformer.py:31-63):
+
+    q, k, v  = rms_norm(x) @ [Wq|Wk|Wv]_r (+ bias)   head-sharded, norm folded in
+    q, k     = rope(q), rope(k); write_kv; attention over this rank's kv heads
+    x        = x + all_reduce(attn @ Wo_r)            fused reduce + residual
+    x        = x + all_reduce(silu(n @ Wg_r) * (n @ Wu_r) @ Wd_r)
+
+The KV caches hold ``kv_heads / world`` heads per rank (tensor_parallel.py:76-79).
+``lm_head`` is vocab-parallel: rank r holds columns ``[r V/w, (r+1) V/w)``;
+``logits_on_device`` gathers the full row on every rank (each rank adds its
+slice into a zeroed ``[B, V]`` buffer and the buffer is all-reduced: adding
+zeros is exact, so this is a concatenation).  The lm_head is not quantized
+unless ``quantize_lm_head`` (the reference's default, ie/quant/model.py:58-63);
+the dense slice is a plain cuBLAS GEMM.  Sampling runs on the device
+(torch_transformer.py:131-140); under TP the tokens of rank 0 are broadcast
+the same way, so every rank continues with identical tokens.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .attention import (FLASH, allocate_kv_cache, apply_rope, flash_decode, flash_prefill,
+                        paged_attention, write_kv)
+from .device import require_cuda
+from .sharding import Shard
+from .tensor_parallel import (ShardedAttention, ShardedMLP, kv_heads_per_rank, quantized_block,
+                              rms_norm)
+
+
+class QuantizedTransformer:
+    def __init__(self, source, *, scheme: str = "int8", axis: int | None = 0,
+                 shard: Shard | None = None, comm=None, device="cuda", dtype=None,
+                 quantize_lm_head: bool = False) -> None:
+        torch = require_cuda()
+        self.config = source.config
+        self.shard = shard or Shard(0, 1)
+        self.world = self.shard.world_size
+        self.comm = comm
+        if self.world > 1 and comm is None:
+            raise ValueError("a tensor-parallel rank needs a Communicator (comm=)")
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.dtype = dtype or torch.float16
+        self.scheme = scheme
+        kv_heads_per_rank(self.config, self.world)   # raises like the reference
+        take = lambda w, dt=None: torch.from_numpy(np.ascontiguousarray(w)).to(
+            device=self.device, dtype=dt or self.dtype)
+        self.embedding = take(source.embedding)
+        self.attn, self.mlp = [], []
+        for block in source.blocks:
+            qb = quantized_block(block, scheme, axis)
+            self.attn.append(ShardedAttention(qb, self.shard, device=self.device))
+            self.mlp.append(ShardedMLP(qb, self.shard, device=self.device))
+            torch.cuda.empty_cache()
+        self.final_norm = take(source.final_norm, torch.float32)
+        vocab = self.config.vocab_size
+        cols = self.shard.slice_of(vocab)
+        self.vocab_slice = cols
+        self.lm_head_packed = None
+        if quantize_lm_head:
+            from .quant_model import quantize_for_device
+            from .sharding import split_output_dim
+
+            q = quantize_for_device(np.asarray(source.lm_head, np.float32), scheme, axis)
+            self.lm_head_packed = split_output_dim(q, self.shard).packed(self.device)
+            self.lm_head = None
+        else:
+            self.lm_head = take(np.asarray(source.lm_head)[:, cols])
+        self.cos = take(source.cos, torch.float32)
+        self.sin = take(source.sin, torch.float32)
+        self.graphs = None
+        self.num_heads = self.config.num_heads // self.world
+        self.num_kv_heads = self.config.num_kv_heads // self.world
+
+    # ---- engine protocol ------------------------------------------------------
+    def allocate_caches(self, num_blocks: int, block_size: int):
+        """ie/model/torch_transformer.py:82-86 with this rank's kv heads."""
+        pairs = [allocate_kv_cache(num_blocks, block_size, self.num_kv_heads,
+                                   self.config.head_dim, self.device, self.dtype)
+                 for _ in range(self.config.num_layers)]
+        return [p[0] for p in pairs], [p[1] for p in pairs]
+
+    @property
+    def uses_flash(self) -> bool:
+        torch = require_cuda()
+        return FLASH and self.dtype in (torch.float16, torch.bfloat16)
+
+    def _reduce(self):
+        return self.comm if self.world > 1 else None
+
+    def _layer(self, i, x, positions, block_tables, plan, layout, k_cache, v_cache,
+               block_size):
+        from .linear import qlinear
+
+        attn, mlp = self.attn[i], self.mlp[i]
+        q, k, v = attn.project_qkv(x)
+        q = apply_rope(q, positions, self.cos, self.sin, attn.rope_halved)
+        k = apply_rope(k, positions, self.cos, self.sin, attn.rope_halved)
+        write_kv(k, v, k_cache, v_cache, plan["slots"])
+        if plan["flash"]:
+            if layout.is_prefill:
+                attended = flash_prefill(q, k, v, k_cache, v_cache, plan["cu_q"], plan["cu_k"],
+                                         layout.max_query_len, layout.max_context_len,
+                                         plan["paged_tables"], block_size, plan["scale"])
+            else:
+                attended = flash_decode(q, k_cache, v_cache, block_tables.int(),
+                                        plan["context_lens"], block_size, plan["scale"])
+        else:
+            attended = paged_attention(q, k_cache, v_cache, block_tables, layout.context_lens,
+                                       layout.query_lens, block_size)
+        a = attended.reshape(-1, self.num_heads * self.config.head_dim).to(x.dtype).contiguous()
+        x = qlinear(a, attn.o_proj, residual=x, comm=self._reduce())
+        from .linear import fuse_norm_pays
+
+        if fuse_norm_pays(x, mlp.gate_up):
+            hidden = qlinear(x, mlp.gate_up, silu_mul=True, norm_weight=mlp.norm,
+                             norm_eps=mlp.eps)
+        else:
+            hidden = qlinear(rms_norm(x, mlp.norm, mlp.eps), mlp.gate_up, silu_mul=True)
+        return qlinear(hidden, mlp.down, residual=x, comm=self._reduce(), out_dtype=x.dtype)
+
+    def run(self, tokens, positions, block_tables, plan, layout, k_caches, v_caches,
+            block_size: int):
+        """ie/model/torch_transformer.py:92-98."""
+        x = self.embedding.index_select(0, tokens)
+        for i in range(len(self.attn)):
+            x = self._layer(i, x, positions, block_tables, plan, layout, k_caches[i],
+                            v_caches[i], block_size)
+        return rms_norm(x, self.final_norm, self.config.norm_eps)
+
+    def forward(self, layout, k_caches, v_caches, block_size: int):
+        """ie/model/torch_transformer.py:100-122."""
+        torch = require_cuda()
+        if self.graphs is not None and self.graphs.can_replay(layout):
+            return self.graphs.replay(layout, k_caches, v_caches)
+        as_tensor = lambda values, dtype=torch.long: torch.as_tensor(
+            np.asarray(values), device=self.device, dtype=dtype)
+        tokens = as_tensor(layout.token_ids)
+        positions = as_tensor(layout.positions)
+        block_tables = as_tensor(layout.block_tables)
+        use_flash = self.uses_flash
+        plan = {
+            "flash": use_flash,
+            "scale": self.config.head_dim ** -0.5,
+            "slots": as_tensor(layout.slot_mapping),
+            "cu_q": as_tensor(layout.cu_seqlens_q, torch.int32) if use_flash else None,
+            "cu_k": as_tensor(layout.cu_seqlens_k, torch.int32) if use_flash else None,
+            "context_lens": as_tensor(layout.context_lens, torch.int32) if use_flash else None,
+            "paged_tables": (block_tables.to(torch.int32)
+                             if use_flash and layout.max_context_len > layout.max_query_len
+                             else None),
+        }
+        return self.run(tokens, positions, block_tables, plan, layout, k_caches, v_caches,
+                        block_size)
+
+    def logits_on_device(self, hidden, query_lens) -> "torch.Tensor":
+        """Full-vocabulary logits of each sequence's last token, on every rank."""
+        torch = require_cuda()
+        ends = torch.as_tensor(np.cumsum(query_lens) - 1, device=self.device, dtype=torch.long)
+        h = hidden.index_select(0, ends)
+        if self.lm_head_packed is not None:
+            from .linear import qlinear
+
+            local = qlinear(h.contiguous(), self.lm_head_packed, out_dtype=torch.float32)
+        else:
+            local = (h @ self.lm_head).float()
+        if self.world == 1:
+            return local
+        full = torch.zeros((h.shape[0], self.config.vocab_size), dtype=torch.float32,
+                           device=self.device)
+        full[:, self.vocab_slice] = local
+        return self.comm.all_reduce(full)
+
+    def logits_for_last_token_of_each(self, hidden, query_lens) -> np.ndarray:
+        return self.logits_on_device(hidden, query_lens).float().cpu().numpy()
+
+    def sample(self, hidden, query_lens, temperatures) -> list[int]:
+        """ie/model/torch_transformer.py:131-140: argmax for temperature 0, else
+        the exponential race over softmax(logits / T); rank 0's choice wins."""
+        torch = require_cuda()
+        logits = self.logits_on_device(hidden, query_lens)
+        temps = torch.as_tensor(np.asarray(temperatures, dtype=np.float32), device=self.device)
+        greedy = temps <= 0.0
+        safe = torch.where(greedy, torch.ones_like(temps), temps).unsqueeze(1)
+        probs = torch.softmax(logits / safe, dim=-1)
+        race = torch.empty_like(probs).exponential_(1.0).clamp_min(1e-10)
+        sampled = (probs / race).argmax(dim=-1)
+        chosen = torch.where(greedy, logits.argmax(dim=-1), sampled)
+        if self.world > 1 and not bool(greedy.all()):
+            mine = chosen.to(torch.float32) if self.shard.rank == 0 else torch.zeros_like(
+                chosen, dtype=torch.float32)
+            chosen = self.comm.all_reduce(mine).round().long()
+        return chosen.tolist()

@@ -126,20 +126,23 @@ def split_heads(weight, shard: Shard, num_heads: int, head_dim: int):
 
 
 def all_reduce(partials):
-    """ie/parallel/sharding.py:40-44 -- ``partials[0] + partials[1] + ...`` in rank
-    order with f32 arithmetic, on the GPU.  NumPy partials come back as NumPy."""
-    torch = require_cuda()
+    """ie/parallel/sharding.py:40-44 -- ``partials[0] + partials[1] + ...`` in rank order.
+
+    NumPy partials keep the reference's exact semantics: a copy of the first,
+    then ``+=`` of the others in rank order, in the partials' own dtype, on the
+    host (the reference's expert-parallel combine, ie/parallel/expert_parallel.py:57,
+    sums NumPy lists through this function).  CUDA tensors are summed on the GPU
+    by ``ie_reduce_partials`` (f32 arithmetic, rank order) and stay on the device."""
     if not partials:
         raise ValueError("all_reduce needs at least one partial")
-    was_numpy = isinstance(partials[0], np.ndarray)
-    if was_numpy:
-        dtype = partials[0].dtype
-        if dtype != np.float32:
-            raise ValueError(f"all_reduce on the device takes float32 partials, got {dtype}")
-        ts = [torch.from_numpy(np.ascontiguousarray(p, dtype=np.float32)).cuda() for p in partials]
-    else:
-        dev = partials[0].device if partials[0].is_cuda else torch.device("cuda")
-        ts = [p.to(dev).contiguous() for p in partials]
+    if isinstance(partials[0], np.ndarray) or np.isscalar(partials[0]):
+        total = np.array(partials[0], copy=True)
+        for part in partials[1:]:
+            total += part
+        return total
+    torch = require_cuda()
+    dev = partials[0].device if partials[0].is_cuda else torch.device("cuda")
+    ts = [p.to(dev).contiguous() for p in partials]
     shape = ts[0].shape
     for t in ts[1:]:
         if t.shape != shape or t.dtype != ts[0].dtype:
@@ -149,7 +152,7 @@ def all_reduce(partials):
     _lib.check(_lib.lib().ie_reduce_partials(arr, len(ts), out.data_ptr(), out.numel(),
                                              dtype_code(out.dtype), _lib.stream_ptr()),
                "all_reduce")
-    return out.cpu().numpy() if was_numpy else out
+    return out
 
 
 def all_gather(partials, axis: int = -1):

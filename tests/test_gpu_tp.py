@@ -68,8 +68,9 @@ def test_sharded_mlp_matches_the_golden_tp_output(golden, world):
     for name in qs:
         np.testing.assert_allclose(qs[name].dequantized(), golden[f"mlp_{name}"], rtol=1e-6)
     xt = torch.from_numpy(x).cuda()
-    partials = [ShardedMLP(np.ones(64, np.float32), qs["gate"], qs["up"], qs["down"],
-                           Shard(r, world)).forward(xt) for r in range(world)]
+    partials = [ShardedMLP.from_weights(np.ones(64, np.float32), qs["gate"], qs["up"],
+                                        qs["down"], Shard(r, world)).forward(xt)
+                for r in range(world)]
     got = (xt + all_reduce(partials)).cpu().numpy()
     np.testing.assert_allclose(got, golden[f"mlp_out_{world}"], rtol=1e-4, atol=1e-5)
 
@@ -81,8 +82,8 @@ def test_full_size_cpu_case_tp2(golden_hashes, dtype):
     qs = {n: W.quantize_integer(w, F.INT8) for n, w in (("gate", gate), ("up", up),
                                                         ("down", down))}
     xt = torch.from_numpy(x).cuda().to(dtype)
-    parts = [ShardedMLP(norm, qs["gate"], qs["up"], qs["down"], Shard(r, 2)).forward(xt)
-             for r in range(2)]
+    parts = [ShardedMLP.from_weights(norm, qs["gate"], qs["up"], qs["down"],
+                                     Shard(r, 2)).forward(xt) for r in range(2)]
     got = (xt.float() + all_reduce([p.float() for p in parts])).cpu().numpy()
     deq = {n: q.dequantized() for n, q in qs.items()}
     want = o.tp_mlp(xt.float().cpu().numpy(), norm, deq["gate"], deq["up"], deq["down"], 2)

@@ -150,3 +150,23 @@ def test_compression_accounting_matches_the_reference():
     q4 = o.quantize_integer(w, 4, True, 0)
     assert _qw(q8.codes, q8.scale).compression == pytest.approx(4.0, rel=0.05)
     assert _qw(q4.codes, q4.scale, bits=4).compression == pytest.approx(8.0, rel=0.05)
+
+
+def test_all_reduce_on_numpy_lists_is_the_references_host_sum():
+    """ie/parallel/sharding.py:40-44: a copy of the first partial, then += in
+    rank order, in the partials' dtype, with no GPU (expert parallelism sums
+    NumPy lists through it, ie/parallel/expert_parallel.py:57)."""
+    from ie_tpq.sharding import all_reduce
+    from oracle import tpq_oracle as o
+
+    parts = [o.seeded_activations(7, 33, seed=s) for s in range(4)]
+    got = all_reduce(parts)
+    assert got.dtype == np.float32 and np.array_equal(got, o.all_reduce(parts))
+    assert got is not parts[0] and not np.shares_memory(got, parts[0])
+    ints = [np.arange(6, dtype=np.int64) * (r + 1) for r in range(3)]
+    assert all_reduce(ints).dtype == np.int64
+    assert np.array_equal(all_reduce(ints), np.arange(6) * 6)
+    f64 = [np.full(3, 0.1, np.float64)] * 3
+    assert all_reduce(f64).dtype == np.float64
+    with pytest.raises(ValueError):
+        all_reduce([])

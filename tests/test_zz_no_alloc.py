@@ -1,8 +1,11 @@
 """ie_qlinear_noalloc, called through the C ABI: the tensor-core quantized
 linear with its split-K partials and tile tickets in the library's static
-device array instead of a caller workspace.  Two calls in a row must each
-match ie_qlinear (caller workspace, the same kernel and split plan) within the
-north-star tolerance rtol 2e-2 / atol 2e-3, and equal each other bitwise.
+device array instead of a caller workspace -- for callers that cannot
+allocate device memory when they run a layer.  Two calls in a row must each
+match ie_qlinear (caller workspace, the same kernel and split plan) and the
+CPU oracle's dequantize-then-matmul within the north-star tolerance
+rtol 2e-2 / atol 2e-3, equal each other bitwise, and leave the device's free
+memory unchanged.
 
 The file name sorts last so that the module also runs after every other GPU
 test in one process; it passes alone in a fresh process as well."""
@@ -52,22 +55,30 @@ def split_k_bytes(a) -> int:
 ])
 def test_two_calls_in_a_row_match_the_workspace_entry_point(scheme, k, n, m):
     w = o.seeded_weight(k, n, seed=k + n + m)
-    q, _ = quantize(scheme, w)
+    q, ref_w = quantize(scheme, w)
     p = q.packed()
     x = torch.from_numpy(o.seeded_activations(m, k, seed=m + 7)).cuda().to(torch.bfloat16)
     res = torch.from_numpy(o.seeded_activations(m, n, seed=m + 8)).cuda().to(torch.bfloat16)
     want = qlinear(x, p, residual=res, algo=ALGO_TCGEN05).float()
-    outs = []
-    for _ in range(2):
-        out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
-        a = build_args(x, p, out, residual=res, algo=ALGO_TCGEN05)
+    oracle = res.float().cpu().numpy() + x.float().cpu().numpy() @ ref_w
+    outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+            for _ in range(2)]
+    args = [build_args(x, p, out, residual=res, algo=ALGO_TCGEN05) for out in outs]
+    # the first call on a device looks the array up (the module is resident by
+    # then: qlinear above ran a kernel of the same library); measure after it
+    _lib.check(noalloc(args[0]), "qlinear_noalloc")
+    torch.cuda.synchronize()
+    outs[0].fill_(float("nan"))
+    free_before = torch.cuda.mem_get_info()[0]
+    for a in args:
         assert 0 < split_k_bytes(a) <= _lib.IE_QLINEAR_NOALLOC_SCRATCH_BYTES
         _lib.check(noalloc(a), "qlinear_noalloc")
-        outs.append(out)
     torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
     for out in outs:
-        np.testing.assert_allclose(out.float().cpu().numpy(), want.cpu().numpy(),
-                                   rtol=RTOL, atol=ATOL)
+        got = out.float().cpu().numpy()
+        np.testing.assert_allclose(got, want.cpu().numpy(), rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(got, oracle, rtol=RTOL, atol=ATOL)
     assert torch.equal(outs[0], outs[1])
     assert status_bits() == 0
 
