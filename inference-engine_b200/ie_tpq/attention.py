@@ -24,6 +24,10 @@ except Exception:  # pragma: no cover - depends on the image
     flash_attn_varlen_func = flash_attn_with_kvcache = None
     FLASH = False
 
+# flash-attn 2.8 rejects a paged KV cache whose page (block) size is not a
+# multiple of 256 ("Paged KV cache block size must be divisible by 256").
+PAGED_FLASH_BLOCK = 256
+
 
 def allocate_kv_cache(num_blocks: int, block_size: int, num_kv_heads: int, head_dim: int,
                       device, dtype):

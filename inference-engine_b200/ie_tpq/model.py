@@ -33,8 +33,8 @@ from __future__ import annotations
 
 import numpy as np
 
-from .attention import (FLASH, allocate_kv_cache, apply_rope, flash_decode, flash_prefill,
-                        paged_attention, write_kv)
+from .attention import (FLASH, PAGED_FLASH_BLOCK, allocate_kv_cache, apply_rope, flash_decode,
+                        flash_prefill, paged_attention, write_kv)
 from .device import require_cuda
 from .sharding import Shard
 from .tensor_parallel import (ShardedAttention, ShardedMLP, kv_heads_per_rank, quantized_block,
@@ -153,7 +153,12 @@ class QuantizedTransformer:
         tokens = as_tensor(layout.token_ids)
         positions = as_tensor(layout.positions)
         block_tables = as_tensor(layout.block_tables)
-        use_flash = self.uses_flash
+        # flash-attn's paged kernels (decode, and prefill over cached context)
+        # take only page sizes that are multiples of PAGED_FLASH_BLOCK; other
+        # block sizes run those steps on the torch paged-attention path.  A
+        # prefill of fresh prompts reads no cache and always takes flash.
+        paged = (not layout.is_prefill) or layout.max_context_len > layout.max_query_len
+        use_flash = self.uses_flash and (not paged or block_size % PAGED_FLASH_BLOCK == 0)
         plan = {
             "flash": use_flash,
             "scale": self.config.head_dim ** -0.5,

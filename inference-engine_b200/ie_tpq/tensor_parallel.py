@@ -85,14 +85,19 @@ def _f32(v, device):
     return t.to(device=device, dtype=torch.float32).contiguous()
 
 
-def quantized_block(block, scheme: str = "int8", axis: int | None = 0):
-    """A view of ``block`` whose seven projections are quantized (reference
-    tables, computed on the device) and whose other attributes are shared.
-    Projections that are already quantized or packed are kept."""
+MLP_PROJECTIONS = ("gate_proj", "up_proj", "down_proj")
+
+
+def quantized_block(block, scheme: str = "int8", axis: int | None = 0,
+                    names: tuple = PROJECTIONS):
+    """A view of ``block`` whose projections ``names`` (all seven by default)
+    are quantized (reference tables, computed on the device) and whose other
+    attributes are shared.  Projections that are already quantized or packed
+    are kept."""
     from .quant_model import quantize_for_device
 
     attrs = {}
-    for name in PROJECTIONS:
+    for name in names:
         w = getattr(block, name)
         attrs[name] = w if isinstance(w, (QuantizedWeight, PackedWeight)) else \
             quantize_for_device(np.asarray(w, dtype=np.float32), scheme, axis)
@@ -231,8 +236,8 @@ class ShardedMLP:
     def __init__(self, block, shard: Shard, *, scheme: str = "int8", axis: int | None = 0,
                  device=None) -> None:
         if not all(isinstance(getattr(block, n), (QuantizedWeight, PackedWeight))
-                   for n in ("gate_proj", "up_proj", "down_proj")):
-            block = quantized_block(block, scheme, axis)
+                   for n in MLP_PROJECTIONS):
+            block = quantized_block(block, scheme, axis, names=MLP_PROJECTIONS)
         self._init(block.mlp_norm, block.gate_proj, block.up_proj, block.down_proj, shard,
                    float(block.config.norm_eps), device)
 

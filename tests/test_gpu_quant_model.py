@@ -106,11 +106,17 @@ def test_pack_transformer_shards_match_the_oracle(scheme, world):
         np.testing.assert_allclose(packed["down"].dequantize().cpu().numpy(), want_d, **tol)
         gu = packed["gate_up"]
         assert gu.gate_up and gu.n == 2 * cfg.intermediate_size // world
-        # gate/up pairs: the SiLU*up product of the packed pair equals the oracle's
+        # gate/up pairs: the pair's columns are the oracle's gate and up shards
+        # (rows interleaved), and its fused SiLU*up product with f32
+        # activations is the f32 product of those columns
+        gu_deq = gu.dequantize().cpu().numpy()
+        np.testing.assert_allclose(gu_deq[:, 0::2],
+                                   o.split_output_dim(deq(blk.gate_proj), r, world), **tol)
+        np.testing.assert_allclose(gu_deq[:, 1::2],
+                                   o.split_output_dim(deq(blk.up_proj), r, world), **tol)
         xt = torch.from_numpy(x).cuda()
         from ie_tpq.linear import qlinear
 
         got = qlinear(xt, gu).cpu().numpy()
-        g = x @ o.split_output_dim(deq(blk.gate_proj), r, world)
-        u = x @ o.split_output_dim(deq(blk.up_proj), r, world)
+        g, u = x @ gu_deq[:, 0::2], x @ gu_deq[:, 1::2]
         np.testing.assert_allclose(got, o.silu(g) * u, rtol=1e-3, atol=1e-4)
