@@ -153,10 +153,15 @@ int ie_dequantize(const ie_qweight* w, int32_t layout, int32_t out_dtype, void* 
  * (ie/parallel/sharding.py:51-66) and the projections of TorchBlock.forward
  * (ie/model/torch_transformer.py:36-38,60) and torch_backend.swiglu
  * (ie/kernels/torch_backend.py:125-127) on a packed shard. */
-/* Bytes of caller-owned workspace the call would use (split-K partials and
- * tile tickets of the tensor-core kernel); the first 256-byte-rounded region
- * holds the tickets, which the call clears on the stream before the kernel
- * runs (so a launch that gave up on an expired wait leaves nothing behind). */
+/* Bytes of caller-owned workspace the call would use with the tensor-core
+ * kernel: 256 bytes of grid-barrier words (offset 0), the split-K tile
+ * tickets, the activations converted once per launch (bf16 -> f16, RMS norm
+ * folded in) and the split-K partials.  The workspace must be zero-filled
+ * before its first use; afterwards the barrier words stay consistent by
+ * themselves (also after a launch that gave up on an expired wait), and the
+ * call clears the tickets on the stream before a split-K kernel runs.  A
+ * smaller workspace (or none) runs the best plan that fits: split-K without
+ * the activation pre-pass, the pre-pass without split-K, or neither. */
 size_t ie_qlinear_workspace_size(const ie_qlinear_args* a);
 int ie_qlinear(const ie_qlinear_args* a, void* stream);
 
@@ -167,9 +172,11 @@ int ie_qlinear(const ie_qlinear_args* a, void* stream);
  * latency-bound decode loop that must never enter the CUDA allocator -- yet
  * want the split-K tensor-core kernel.
  * Same arguments and result as ie_qlinear on the tensor-core path; workspace
- * and workspace_bytes are ignored.  The split-K partials and tile tickets live
- * in a static device array of IE_QLINEAR_NOALLOC_SCRATCH_BYTES inside the
- * library; a call whose plan needs more returns IE_ERR_INVALID, and a call the
+ * and workspace_bytes are ignored.  The split-K partials, tile tickets and the
+ * converted activations of the pre-pass live in a static device array of
+ * IE_QLINEAR_NOALLOC_SCRATCH_BYTES inside the library; a call whose preferred
+ * plan needs more runs the best plan that fits (without split-K, then also
+ * without the pre-pass, which needs no scratch at all).  A call the
  * tensor-core kernel cannot serve (f32 activations, K % 128 != 0, unaligned
  * rows, algo 1) returns IE_ERR_UNSUPPORTED.  The first call on a device looks
  * up that device's copy of the array (cudaGetSymbolAddress, which may load the

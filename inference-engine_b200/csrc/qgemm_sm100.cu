@@ -111,6 +111,16 @@ struct TcParams {
   const float* norm_w;      // null: no prologue
   float norm_eps;
   int nw_off;               // byte offset of a stage's norm weights [sub][128] in its table slot
+  // Activation pre-pass (the XPRE kernels): the CTAs first write the MMA's f16 operand
+  // xh[M][K] (bf16 -> f16, RMS norm applied) into the workspace, each a slice,
+  // then meet at a grid barrier; the x tiles are then TMA-loaded from xh as
+  // they are.  Barrier words: xbar[0] counts this launch's arrivals (the last
+  // arriver sets it back to zero), xbar[1] is a generation the last arriver
+  // advances; waiters wait for it to leave the value read at kernel start.
+  // Every CTA arrives exactly once (at teardown if it gave up before), so
+  // the words are consistent for the next launch without being cleared.
+  __half* xh;
+  uint32_t* xbar;
 };
 
 // ---------------------------------------------------------------------------
@@ -142,7 +152,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait on an mbarrier phase: false (and an error bit) once the SM
-// clock has advanced kWaitCycles, or at once if another role aborted.
+// clock has advanced kWaitCycles, or at once if another role aborted.  (A
+// try_wait with a suspend-time hint was slower: a suspended warp noticed the
+// completed phase late.)
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           const volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -257,6 +269,20 @@ __device__ __forceinline__ uint32_t ticket_add(uint32_t* p) {
   uint32_t old;
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
   return old;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Orders this thread's generic-proxy global accesses with its async-proxy
+// (TMA) accesses: after writing data another CTA's TMA will read, and after
+// acquiring such data before issuing the TMA that reads it.
+__device__ __forceinline__ void fence_proxy_async_all() {
+  asm volatile("fence.proxy.async;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -672,6 +698,52 @@ __device__ __forceinline__ float row_sumsq(const void* row, int64_t K, int x_bf1
   return ss;
 }
 
+// Activation pre-pass of one CTA (the dequant threads, dt = 0 .. kDqThreads-1):
+// chunks [c0, c1) of xh's M*K/8 16-byte chunks, chunk i = token i / (K/8),
+// K values 8 * (i % (K/8)) ...  Each chunk is what the in-loop conversion
+// makes of it: bf16 -> f16 (saturating), or with the RMS norm
+// f16((x * rinv) * w) with the same rinv and products, so xh is bit-identical
+// to the converted x tiles.  The RMS factors of the slice's tokens are
+// computed here, up to kDqWarps tokens per round (one warp each), into s_rinv.
+template <class Sync>
+__device__ __forceinline__ bool xpre_slice(const TcParams& p, int dt, int warp_i, int lane,
+                                           float* s_rinv, int64_t c0, int64_t c1,
+                                           const Sync& dq_sync) {
+  const int64_t cpr = p.K / 8;   // chunks per token row
+  const uint4* x = static_cast<const uint4*>(p.x);
+  uint4* xh = reinterpret_cast<uint4*>(p.xh);
+  const int64_t rs = p.ldx / 8;  // x row stride in chunks
+  if (c1 <= c0) return true;
+  const int64_t t_first = c0 / cpr, t_last = (c1 - 1) / cpr;
+  for (int64_t t0 = t_first; t0 <= t_last; t0 += kDqWarps) {
+    const int64_t t1 = t_last + 1 < t0 + kDqWarps ? t_last + 1 : t0 + kDqWarps;
+    if (p.norm_w) {
+      for (int64_t t = t0 + warp_i; t < t1; t += kDqWarps) {
+        const float ss = row_sumsq(static_cast<const char*>(p.x) + t * p.ldx * 2, p.K, p.x_bf16,
+                                   lane);
+        if (lane == 0)
+          s_rinv[t - t0] = 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.norm_eps));
+      }
+      if (!dq_sync()) return false;
+    }
+    const int64_t a = c0 > t0 * cpr ? c0 : t0 * cpr, b = c1 < t1 * cpr ? c1 : t1 * cpr;
+    for (int64_t i = a + dt; i < b; i += kDqThreads) {
+      const int64_t t = i / cpr, kc = i - t * cpr;
+      uint4 v = __ldcg(x + t * rs + kc);
+      if (p.norm_w) {
+        if (p.x_bf16) norm_chunk<true>(&v, p.norm_w + kc * 8, s_rinv[t - t0]);
+        else norm_chunk<false>(&v, p.norm_w + kc * 8, s_rinv[t - t0]);
+      } else {
+        bf16_to_f16_chunk(&v);
+      }
+      xh[t * cpr + kc] = v;
+    }
+    if (a + dt < b) fence_proxy_async_all();   // these stores, before other CTAs' TMA reads
+    if (p.norm_w && !dq_sync()) return false;   // s_rinv is rewritten next round
+  }
+  return true;
+}
+
 // Epilogue value of token m, row n, before the residual: scale, then bias.
 struct Epi {
   const TcParams& p;
@@ -750,7 +822,10 @@ struct Epi {
 // CSPLIT: the K splits of a tile reduce inside a thread-block cluster instead
 // of through global partials; each instantiation carries only one of the two
 // paths, so neither takes registers from the dequant loop of the other.
-template <int FMT, bool CSPLIT>
+// XPRE: the activation pre-pass (x tiles from xh, loaded on their own
+// barriers once the grid barrier opens); without it the x tiles share the
+// weights' stage barrier and bf16 / RMS-norm tiles are converted in the loop.
+template <int FMT, bool CSPLIT, bool XPRE>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                 const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
@@ -770,9 +845,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint8_t* t_ring = w_ring + ns * p.w_stage_bytes;          // ns x t_stage_bytes
   float* recv = reinterpret_cast<float*>(t_ring + ns * p.t_stage_bytes);   // csplit
   uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + ns * p.t_stage_bytes + p.recv_bytes);
-  uint64_t* full = bars;                 // [ns]  TMA landed (count 1 + tx)
+  uint64_t* full = bars;                 // [ns]  weights + tables landed (count 1 + tx)
   uint64_t* empty = full + ns;           // [ns]  MMA done + every dequant warp done
-  uint64_t* afull = empty + ns;          // [na]  a pair's 4 * kHalves warps wrote A
+  uint64_t* xfull = empty + ns;          // [ns]  XPRE: the stage's x tile landed (count 1 + tx)
+  uint64_t* afull = xfull + ns;          // [na]  a pair's 4 * kHalves warps wrote A
   uint64_t* aempty = afull + na;         // [na]  MMA read A (commit)
   uint64_t* accfull = aempty + na;       // every issuer's MMAs of a unit done -> epilogue
   uint64_t* accempty = accfull + 1;      // epilogue -> MMA (count 1)
@@ -784,6 +860,15 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(abort_flag) + 1;
   float* s_rinv = reinterpret_cast<float*>(s_ticket + 1);   // [bn] RMS-norm prologue
+  // pre-pass barrier: [0] generation at kernel start, [1] this CTA has arrived
+  volatile uint32_t* s_xb = reinterpret_cast<volatile uint32_t*>(s_rinv + p.bn);
+  auto xbar_arrive = [&]() {
+    if (ticket_add(p.xbar) == gridDim.x - 1u) {
+      *reinterpret_cast<volatile uint32_t*>(p.xbar) = 0u;   // ordered by the release below
+      st_release_gpu(p.xbar + 1, s_xb[0] + 1u);
+    }
+    s_xb[1] = 1u;
+  };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t epoch = reduce ? reduce_epoch(rc) : 0u;
@@ -792,6 +877,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], p.issuers + kDqWarps);   // each issuer's commit + every dequant warp
+      mbar_init(&xfull[s], 1);
     }
     for (int s = 0; s < na; ++s) {
       mbar_init(&afull[s], 4 * kHalves);
@@ -804,6 +890,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     mbar_init(rfull, (uint32_t)((p.splits - 1) * kDqWarps));
     mbar_init(rfree, (uint32_t)kDqWarps);
     *abort_flag = 0;
+    if constexpr (XPRE) {   // before any arrival of this CTA, hence before the barrier opens
+      s_xb[0] = ld_acquire_gpu(p.xbar + 1);
+      s_xb[1] = 0u;
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -846,6 +936,13 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
+    // Weights and tables of a stage land on full[s]; its x tile too, or with
+    // XPRE on xfull[s].  With the pre-pass the x tiles come from xh, which is complete
+    // only once every CTA has passed the grid barrier: until then the producer
+    // issues weight stages only (remembering each one's x coordinates) and
+    // waits for the barrier when the ring is full -- reusing a slot needs that
+    // stage's MMAs, hence its x tile, anyway.  (Polling the barrier between
+    // stages put an L2 round trip in front of every early weight copy.)
     if (lane == 0) {
       prefetch_tmap(&tm_w);
       prefetch_tmap(&tm_x);
@@ -855,17 +952,55 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const uint32_t tbytes = p.t_kind == 1 ? (uint32_t)(2 * kTileN * 2 * sub)
                               : (p.t_kind == 2 ? (uint32_t)(p.t_rows * kBK * 4 * sub) : 0u);
       const int row_sub = w_sub_bytes / kTileN;
-      for (int u = u_first; u < u_end && !*abort_flag; u += u_step) {
+      bool xready = !XPRE;
+      int x_next = 0;                 // first stage whose x tile is not issued yet
+      uint32_t pend[12];   // x coordinates (mt << 16 | ks) of stages x_next .. ti, by slot
+      bool ok = true;
+      auto issue_x = [&](int tj, int mt, int ks) {
+        const int sj = tj % ns;
+        mbar_expect_tx(&xfull[sj], (uint32_t)x_stage_bytes);
+        // every 64-wide K block of the stage's activation tile in one copy
+        tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &xfull[sj]);
+      };
+      // x tiles of the remembered stages x_next .. limit - 1
+      auto flush_x = [&](int limit) {
+        for (; x_next < limit; ++x_next)
+          issue_x(x_next, (int)(pend[x_next % ns] >> 16), (int)(pend[x_next % ns] & 0xFFFFu));
+      };
+      auto poll_x = [&](int limit) -> bool {
+        if (!XPRE || xready) return true;
+        const uint32_t gen0 = s_xb[0];
+        if (ld_acquire_gpu(p.xbar + 1) == gen0) {
+          const long long t0 = clock64();
+          while (ld_acquire_gpu(p.xbar + 1) == gen0) {
+            if (*abort_flag) return false;
+            if (clock64() - t0 > kWaitCycles) {
+              atomicOr(&g_tc_status, kErrWait);
+              return false;
+            }
+            __nanosleep(64);
+          }
+        }
+        fence_proxy_async_all();   // xh was written by other CTAs' generic stores
+        xready = true;
+        flush_x(limit);
+        return true;
+      };
+      for (int u = u_first; u < u_end && ok && !*abort_flag; u += u_step) {
         int nt, mt, ks0, ks1, sp;
         unit_range(u, nt, mt, ks0, ks1, sp);
         for (int ks = ks0; ks < ks1; ks += sub, ++ti) {
           const int s = ti % ns;
+          // reusing a slot needs the MMAs of stage ti - ns, hence its x tile
+          if (ti >= ns && !(ok = poll_x(ti))) break;
           if (!mbar_wait(&empty[s], ((ti / ns) & 1) ^ 1, abort_flag)) {
-            *abort_flag = 1;
+            ok = false;
             break;
           }
-          const uint32_t nbytes = p.norm_w ? (uint32_t)(min(sub, p.kstages - ks) * kBK * 4) : 0u;
-          mbar_expect_tx(&full[s], (uint32_t)(p.w_stage_bytes + x_stage_bytes) + tbytes + nbytes);
+          const uint32_t nbytes =
+              (p.norm_w && !XPRE) ? (uint32_t)(min(sub, p.kstages - ks) * kBK * 4) : 0u;
+          mbar_expect_tx(&full[s], (uint32_t)p.w_stage_bytes + tbytes + nbytes +
+                                       (XPRE ? 0u : (uint32_t)x_stage_bytes));
           uint8_t* ws_ = w_ring + s * p.w_stage_bytes;
           for (int j = 0; j < sub; ++j)   // K past the end reads as zeros
             tma_load_2d(ws_ + j * w_sub_bytes, &tm_w, (ks + j) * row_sub, nt * kTileN, &full[s]);
@@ -880,16 +1015,28 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           } else if (p.t_kind == 2) {
             tma_load_3d(ts, &tm_s, 0, ks, 0, &full[s]);               // [rows][sub][128]
           }
-          if (p.norm_w)   // the stage's norm weights, only those inside [0, K)
-            bulk_load(ts + p.nw_off, p.norm_w + (int64_t)ks * kBK,
-                      (uint32_t)(min(sub, p.kstages - ks) * kBK * 4), &full[s]);
-          // every 64-wide K block of the stage's activation tile in one copy
-          tma_load_3d(x_ring + s * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[s]);
+          if (nbytes)   // the stage's norm weights, only those inside [0, K)
+            bulk_load(ts + p.nw_off, p.norm_w + (int64_t)ks * kBK, nbytes, &full[s]);
+          if constexpr (!XPRE) {
+            // every 64-wide K block of the stage's activation tile in one copy
+            tma_load_3d(x_ring + s * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[s]);
+          } else if (xready) {
+            issue_x(ti, mt, ks);
+            x_next = ti + 1;
+          } else {
+            pend[s] = ((uint32_t)mt << 16) | (uint32_t)ks;
+          }
         }
       }
-      // drain: every issued stage's copy must have landed before exit
+      // stages whose x is still pending: the MMA issuers wait for it
+      if (XPRE && ok && ti > x_next) ok = poll_x(ti);
+      if (!ok) *abort_flag = 1;
+      // drain: every issued stage's copies must have landed before exit
       const int first = ti > ns ? ti - ns : 0;
-      for (int j = first; j < ti; ++j) mbar_drain(&full[j % ns], (j / ns) & 1);
+      for (int j = first; j < ti; ++j) {
+        mbar_drain(&full[j % ns], (j / ns) & 1);
+        if (XPRE && j < x_next) mbar_drain(&xfull[j % ns], (j / ns) & 1);
+      }
     }
   } else if (warp <= kMmaWarps) {
     // ------------------------------ MMA issuers -------------------------------
@@ -930,8 +1077,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           const int nsub = min(sub, ks1 - ks);
           const uint32_t x_lo = x_lo0 + s * x_stage16;
           // Every role that arrives on empty[s] first waits for this use of the
-          // stage to land, so no arrival can be credited to an earlier phase.
-          if (!mbar_wait(&full[s], s_ph, abort_flag)) {
+          // stage to land, so no arrival can be credited to an earlier phase;
+          // the issuers wait for the stage's x tile (the B operand).
+          if (!mbar_wait(XPRE ? &xfull[s] : &full[s], s_ph, abort_flag)) {
             ok = false;
             break;
           }
@@ -1004,12 +1152,23 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       dq_ph ^= 1u;
       return done;
     };
+    if constexpr (XPRE) {
+      // Activation pre-pass: this CTA's share of xh, then the grid barrier.
+      // The dequant warps do not wait for the barrier themselves (the weights
+      // need no activations); the producer waits before loading x tiles.
+      const int64_t total = p.M * (p.K / 8);
+      const int64_t g = gridDim.x, b = blockIdx.x;
+      ok = xpre_slice(p, dt, warp - kDqWarp0, lane, s_rinv, total * b / g, total * (b + 1) / g,
+                      dq_sync);
+      if (ok) ok = dq_sync();
+      if (ok && dt == 0) xbar_arrive();
+    }
     int norm_mt = -1;   // token tile whose RMS factors s_rinv holds
     for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
       unit_range(u, nt, mt, ks0, ks1, sp);
       const int64_t n = (int64_t)nt * kTileN + row;
-      if (p.norm_w && mt != norm_mt) {
+      if (p.norm_w && !XPRE && mt != norm_mt) {
         // RMS factors of the tile's tokens over the full K (every split needs
         // them, so each CTA reads the rows itself, from L2): dequant warp w
         // takes tokens w, w + 16, ...  The previous unit's conversions all
@@ -1062,7 +1221,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             dequant_half<FMT>(wst, row, h, tst, p.t_rows, p.axis, n, j, sub, o);
             tmem_st32(tmem_a + lane_addr + aj * (uint32_t)kACols + (uint32_t)(h * 32), o);
           }
-          if (p.norm_w) {
+          if constexpr (XPRE) {
+            // x tiles arrive from xh already converted
+          } else if (p.norm_w) {
             // chunk i of the sub-stage: 128-byte line i / 8 = (64-K block,
             // token), 16-byte column (i % 8) XOR (line % 8) under the
             // 128-byte swizzle (bn is a multiple of 16, so line % 8 is the
@@ -1293,6 +1454,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
   // ------------------------------ teardown ------------------------------
   __syncthreads();
+  // a CTA that gave up before arriving at the pre-pass barrier arrives now, so
+  // the barrier words end every launch consistent (the error bit is set)
+  if constexpr (XPRE) {
+    if (threadIdx.x == 0 && !s_xb[1]) xbar_arrive();
+  }
   // no CTA leaves while another CTA of its cluster may still write to its
   // shared memory or arrive on its barriers
   if constexpr (CSPLIT) cluster_sync();
@@ -1397,9 +1563,13 @@ struct Plan {
   int w_stage_bytes = 0;
   int t_kind = 0, t_rows = 0, t_stage_bytes = 0, nw_off = 0;
   size_t smem = 0;
-  size_t ws_bytes = 0;       // counters + partials
+  size_t ws_bytes = 0;       // counters + pre-pass activations + partials
+  size_t counters_off = 0;   // split-K tile tickets, cleared by every launch that uses them
   size_t counters_bytes = 0;
+  size_t xh_off = 0;         // pre-pass activations xh [M][K] f16
+  size_t part_off = 0;       // split-K partials [splits][M][N] f32
   bool csplit = false;       // splits of a tile as one thread-block cluster
+  bool xpre = false;         // activation pre-pass (bf16 or RMS-norm activations)
   int recv_bytes = 0;
 };
 
@@ -1434,7 +1604,7 @@ int fmt_of(const ie_qweight& w) {
 // minimises the slowest CTA's time in TMA-stage units: the stages of its units,
 // a fixed cost per unit (pipeline drain and epilogue) and per split-K finalize,
 // plus the f32 partials' extra traffic spread over the SMs.
-Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
+Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
   Plan pl;
   pl.fmt = fmt_of(a.w);
   const int64_t M = a.m;
@@ -1442,6 +1612,21 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   pl.m_tiles = (int)((M + pl.bn - 1) / pl.bn);
   pl.n_tiles = (int)((a.w.n + kTileN - 1) / kTileN);
   pl.kstages = (int)(a.w.k / kBK);
+  // Activations that need converting (bf16, or the RMS norm applied) can be
+  // converted once per launch into the workspace (xh) instead of once per work
+  // unit inside every CTA, at the price of a grid barrier before the first
+  // MMA.  Measured on B200 (Llama-3-8B shapes, int4-g128) it pays for folded
+  // norms above 16 tokens (each unit otherwise re-reads its tokens' rows for
+  // the RMS factors: qkv 32.8 -> 28.7 us, gate/up 65.9 -> 48.9 us at 64
+  // tokens) and for plain bf16 launches whose repeated conversion is large
+  // (gate/up at 64 tokens 51.2 -> 47.5 us); at 16 tokens and on small grids
+  // the barrier costs more (o 13.2 -> 16.9 us).
+  {
+    const bool norm = (a.epilogue & IE_EPI_RMS_NORM) != 0;
+    const double per_sm = (double)pl.n_tiles * (double)M * (double)a.w.k / sm_count();
+    const bool pays = norm ? M > 16 : per_sm >= 256.0 * 1024.0;
+    pl.xpre = allow_xpre && (a.act_dtype == IE_DT_BF16 || norm) && pays;
+  }
   const int row_stage = (pl.fmt == F_INT4G || pl.fmt == F_INT4SYM) ? kBK / 2 : kBK;
   // a TMA stage carries 32 KB of weights (4 int4 groups or 2 8-bit ones) when the
   // token tile leaves room: large stages amortise the barrier round trips
@@ -1491,9 +1676,10 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
     pl.t_rows = a.w.gate_up ? 2 : 1;
     tbytes = pl.t_rows * kBK * 4 * pl.sub;
   }
-  // the RMS-norm weights of a stage follow its tables in the same slot
+  // the RMS-norm weights of a stage follow its tables in the same slot (only
+  // when the x tiles are normalised in the loop, not by the pre-pass)
   pl.nw_off = (tbytes + 15) / 16 * 16;
-  if (a.epilogue & IE_EPI_RMS_NORM) tbytes = pl.nw_off + kBK * 4 * pl.sub;
+  if ((a.epilogue & IE_EPI_RMS_NORM) && !pl.xpre) tbytes = pl.nw_off + kBK * 4 * pl.sub;
   pl.t_stage_bytes = (tbytes + 1023) / 1024 * 1024;
   // TMEM: accumulators, then the A ring (64 columns a sub-stage).  Narrow token
   // tiles rotate their MMAs over independent accumulator chains, and two issuing
@@ -1526,13 +1712,32 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split) {
   pl.ns = (int)std::min<size_t>(12, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
   // barriers, then TMEM slot, abort flag, ticket and the RMS factors [bn]
-  pl.smem = fixed + (size_t)pl.ns * per + 8 * (2 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 3) + 16 +
-            4 * (size_t)pl.bn;
+  pl.smem = fixed + (size_t)pl.ns * per + 8 * (3 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 3) + 16 +
+            4 * (size_t)pl.bn + 8;
   if (pl.smem < (size_t)kMinSmem) pl.smem = kMinSmem;   // one CTA per SM: TMEM and co-residency
-  if (pl.splits > 1 && !pl.csplit) {
-    pl.counters_bytes = (((size_t)tiles * 4) + 255) / 256 * 256;
-    pl.ws_bytes = pl.counters_bytes + (size_t)pl.splits * M * a.w.n * 4;
-  }
+  // workspace: [pre-pass barrier words, 256 B | tile tickets | xh | split-K
+  // partials].  The barrier words sit at offset 0 for every plan and keep
+  // themselves consistent (zero on first use); the tickets are cleared by
+  // every launch that uses them.
+  const bool global_split = pl.splits > 1 && !pl.csplit;
+  pl.counters_off = 256;
+  pl.counters_bytes = global_split ? ((size_t)tiles * 4 + 255) / 256 * 256 : 0;
+  pl.xh_off = pl.counters_off + pl.counters_bytes;
+  const size_t xh_bytes = pl.xpre ? ((size_t)M * a.w.k * 2 + 255) / 256 * 256 : 0;
+  pl.part_off = pl.xh_off + xh_bytes;
+  const size_t part_bytes = global_split ? (size_t)pl.splits * M * a.w.n * 4 : 0;
+  pl.ws_bytes = (global_split || pl.xpre) ? pl.part_off + part_bytes : 0;
+  return pl;
+}
+
+// The best plan whose workspace fits in `avail` bytes: split-K and the
+// activation pre-pass, then split-K alone (cluster split-K needs no
+// workspace), then the pre-pass alone, then neither.
+Plan fitting_plan(const ie_qlinear_args& a, size_t avail) {
+  Plan pl = make_plan(a, true, true);
+  if (pl.ws_bytes > avail) pl = make_plan(a, true, false);
+  if (pl.ws_bytes > avail) pl = make_plan(a, false, true);
+  if (pl.ws_bytes > avail) pl = make_plan(a, false, false);
   return pl;
 }
 
@@ -1551,7 +1756,10 @@ template <int FMT>
 int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw,
                  const CUtensorMap& tx, const CUtensorMap& ts, const CUtensorMap& tz,
                  const TcParams& prm, const ReduceCtx* rc, cudaStream_t s) {
-  auto kern = pl.csplit ? qgemm_tc_kernel<FMT, true> : qgemm_tc_kernel<FMT, false>;
+  auto kern = pl.csplit ? (pl.xpre ? qgemm_tc_kernel<FMT, true, true>
+                                    : qgemm_tc_kernel<FMT, true, false>)
+                        : (pl.xpre ? qgemm_tc_kernel<FMT, false, true>
+                                   : qgemm_tc_kernel<FMT, false, false>);
   IE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)pl.smem));
   const int units = pl.n_tiles * pl.m_tiles * pl.splits;
@@ -1615,13 +1823,13 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
 
 size_t tc_workspace_bytes(const ie_qlinear_args& a) {
   if (!tc::tc_eligible(a)) return 0;
-  return tc::make_plan(a, true).ws_bytes;
+  return tc::make_plan(a, true, true).ws_bytes;
 }
 
 bool tc_usable(const ie_qlinear_args& a) { return tc::tc_eligible(a); }
 
 int64_t tc_tiles(const ie_qlinear_args& a) {
-  const tc::Plan pl = tc::make_plan(a, a.workspace != nullptr);
+  const tc::Plan pl = tc::fitting_plan(a, a.workspace ? a.workspace_bytes : 0);
   return (int64_t)pl.n_tiles * pl.m_tiles;
 }
 
@@ -1630,8 +1838,7 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   IE_CHECK(tc_eligible(a), "qlinear: the tensor-core path needs bf16/f16 activations, K %% 128 "
                            "== 0, 16-byte aligned rows (and norm weight) and the driver's TMA "
                            "encoder");
-  Plan pl = make_plan(a, true);
-  if (pl.ws_bytes > 0 && (!a.workspace || a.workspace_bytes < pl.ws_bytes)) pl = make_plan(a, false);
+  const Plan pl = fitting_plan(a, a.workspace ? a.workspace_bytes : 0);
   EncodeFn enc = encode_fn();
   CUtensorMap tw, tx;
   {
@@ -1650,15 +1857,20 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(weights): %d", (int)r);
   }
+  char* ws = static_cast<char*>(a.workspace);
   {
-    // x viewed as [K/64][M][64]: one box {64, BN, 2} is a stage's two SW128 blocks
+    // x viewed as [K/64][M][64]: one box {64, BN, 2} is a stage's two SW128 blocks;
+    // with the pre-pass the tiles come from xh (f16, rows of K)
+    const int64_t ld = pl.xpre ? a.w.k : a.ldx;
     const cuuint64_t dims[3] = {64, (cuuint64_t)a.m, (cuuint64_t)(a.w.k / 64)};
-    const cuuint64_t strides[2] = {(cuuint64_t)a.ldx * 2, 128};
+    const cuuint64_t strides[2] = {(cuuint64_t)ld * 2, 128};
     const cuuint32_t box[3] = {64, (cuuint32_t)pl.bn, (cuuint32_t)(2 * pl.sub)};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUtensorMapDataType dt = a.act_dtype == IE_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUresult r = enc(&tx, dt, 3, const_cast<void*>(a.x), dims, strides, box, estr,
+    const CUtensorMapDataType dt = (a.act_dtype == IE_DT_BF16 && !pl.xpre)
+                                       ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    void* base = pl.xpre ? static_cast<void*>(ws + pl.xh_off) : const_cast<void*>(a.x);
+    CUresult r = enc(&tx, dt, 3, base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(IE_ERR_CUDA, "cuTensorMapEncodeTiled(x): %d", (int)r);
@@ -1733,22 +1945,28 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   prm.csplit = pl.csplit ? 1 : 0;
   prm.recv_bytes = pl.recv_bytes;
   if (pl.splits > 1 && !pl.csplit) {
-    prm.counters = static_cast<uint32_t*>(a.workspace);
-    prm.ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pl.counters_bytes);
+    prm.counters = reinterpret_cast<uint32_t*>(ws + pl.counters_off);
+    prm.ws = reinterpret_cast<float*>(ws + pl.part_off);
     // The finalizing CTA of a tile resets its ticket, but a launch that gave up
     // on an expired wait leaves the tickets of its unfinished tiles counted; a
     // later launch on the same workspace would then finalize a tile before all
     // of its splits arrived.  Clearing them first makes every launch start
     // from zero whatever happened before.
-    IE_CUDA_TRY(cudaMemsetAsync(a.workspace, 0, pl.counters_bytes, s));
+    IE_CUDA_TRY(cudaMemsetAsync(ws + pl.counters_off, 0, pl.counters_bytes, s));
   }
   prm.x_bf16 = a.act_dtype == IE_DT_BF16 ? 1 : 0;
   if (a.epilogue & IE_EPI_RMS_NORM) {
-    prm.x = a.x;
-    prm.ldx = a.ldx;
     prm.norm_w = a.norm_weight;
     prm.norm_eps = a.norm_eps;
     prm.nw_off = pl.nw_off;
+  }
+  if ((a.epilogue & IE_EPI_RMS_NORM) || pl.xpre) {
+    prm.x = a.x;
+    prm.ldx = a.ldx;
+  }
+  if (pl.xpre) {
+    prm.xh = reinterpret_cast<__half*>(ws + pl.xh_off);
+    prm.xbar = reinterpret_cast<uint32_t*>(ws);
   }
   switch (pl.fmt) {
     case F_INT4G: return launch_typed<F_INT4G>(a, pl, tw, tx, ts, tz, prm, rc, s);
@@ -1810,18 +2028,14 @@ int launch_qlinear_tc_static(const ie_qlinear_args& a, cudaStream_t s) {
     return set_error(IE_ERR_UNSUPPORTED,
                      "qlinear_noalloc: only the tensor-core path is served (bf16/f16 "
                      "activations, K %% 128 == 0, 16-byte aligned rows, algo 0 or 2)");
-  const Plan pl = make_plan(a, true);
-  if (pl.ws_bytes > IE_QLINEAR_NOALLOC_SCRATCH_BYTES)
-    return set_error(IE_ERR_INVALID,
-                     "qlinear_noalloc: %lld tokens x %lld rows need %zu bytes of split-K "
-                     "scratch; the static scratch holds %zu (use ie_qlinear with a workspace)",
-                     (long long)a.m, (long long)a.w.n, pl.ws_bytes,
-                     (size_t)IE_QLINEAR_NOALLOC_SCRATCH_BYTES);
   ie_qlinear_args b = a;
   b.workspace = scratch;
   b.workspace_bytes = IE_QLINEAR_NOALLOC_SCRATCH_BYTES;
-  // launch_qlinear_tc clears the tile tickets at the start of the array before
-  // a split-K launch, so they read zero even after a call that ended early
+  // launch_qlinear_tc runs the best plan whose scratch fits in the array
+  // (fitting_plan: split-K and the activation pre-pass, the pre-pass alone, or
+  // neither) and clears the tile tickets first, so they read zero even after a
+  // call that ended early; the pre-pass barrier words (zero at module load)
+  // keep themselves consistent
   return launch_qlinear_tc(b, nullptr, s);
 }
 
