@@ -121,6 +121,11 @@ struct TcParams {
   // the words are consistent for the next launch without being cleared.
   __half* xh;
   uint32_t* xbar;
+  // Launched as a programmatic dependent of the previous kernel on the stream:
+  // the prologue and the first weight stages overlap that kernel's tail, and
+  // nothing it writes (x, the residual, RMS-norm rows, the all-reduce epoch,
+  // the workspace) is read or written before griddepcontrol.wait.
+  int pdl;
 };
 
 // ---------------------------------------------------------------------------
@@ -283,6 +288,15 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
 // acquiring such data before issuing the TMA that reads it.
 __device__ __forceinline__ void fence_proxy_async_all() {
   asm volatile("fence.proxy.async;" ::: "memory");
+}
+// Programmatic dependent launch: let the next kernel on the stream launch (its
+// CTAs take SMs as this grid's CTAs exit), and wait for the previous kernel to
+// complete with its memory visible (a no-op without a programmatic edge).
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -871,6 +885,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  // The all-reduce epoch, the pre-pass barrier generation and the pre-pass's
+  // reads of x all depend on the previous kernel: such launches wait at once.
+  // The others overlap their prologue and first weight stages with it.
+  if (reduce || XPRE) pdl_wait();
   const uint32_t epoch = reduce ? reduce_epoch(rc) : 0u;
 
   if (threadIdx.x == 0) {
@@ -952,15 +971,19 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const uint32_t tbytes = p.t_kind == 1 ? (uint32_t)(2 * kTileN * 2 * sub)
                               : (p.t_kind == 2 ? (uint32_t)(p.t_rows * kBK * 4 * sub) : 0u);
       const int row_sub = w_sub_bytes / kTileN;
-      bool xready = !XPRE;
+      bool xready = !XPRE && !p.pdl;
       int x_next = 0;                 // first stage whose x tile is not issued yet
       uint32_t pend[12];   // x coordinates (mt << 16 | ks) of stages x_next .. ti, by slot
       bool ok = true;
       auto issue_x = [&](int tj, int mt, int ks) {
         const int sj = tj % ns;
-        mbar_expect_tx(&xfull[sj], (uint32_t)x_stage_bytes);
         // every 64-wide K block of the stage's activation tile in one copy
-        tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &xfull[sj]);
+        if constexpr (XPRE) {
+          mbar_expect_tx(&xfull[sj], (uint32_t)x_stage_bytes);
+          tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &xfull[sj]);
+        } else {   // the stage's full barrier already expects these bytes
+          tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[sj]);
+        }
       };
       // x tiles of the remembered stages x_next .. limit - 1
       auto flush_x = [&](int limit) {
@@ -968,7 +991,13 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           issue_x(x_next, (int)(pend[x_next % ns] >> 16), (int)(pend[x_next % ns] & 0xFFFFu));
       };
       auto poll_x = [&](int limit) -> bool {
-        if (!XPRE || xready) return true;
+        if (xready) return true;
+        if constexpr (!XPRE) {   // programmatic launch: x is the previous kernel's output
+          pdl_wait();
+          xready = true;
+          flush_x(limit);
+          return true;
+        }
         const uint32_t gen0 = s_xb[0];
         if (ld_acquire_gpu(p.xbar + 1) == gen0) {
           const long long t0 = clock64();
@@ -1017,10 +1046,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           }
           if (nbytes)   // the stage's norm weights, only those inside [0, K)
             bulk_load(ts + p.nw_off, p.norm_w + (int64_t)ks * kBK, nbytes, &full[s]);
-          if constexpr (!XPRE) {
-            // every 64-wide K block of the stage's activation tile in one copy
-            tma_load_3d(x_ring + s * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[s]);
-          } else if (xready) {
+          if (xready) {
             issue_x(ti, mt, ks);
             x_next = ti + 1;
           } else {
@@ -1028,8 +1054,16 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           }
         }
       }
-      // stages whose x is still pending: the MMA issuers wait for it
-      if (XPRE && ok && ti > x_next) ok = poll_x(ti);
+      // stages whose x is still pending: the MMA issuers wait for it.  Without
+      // the pre-pass their full barriers expect the x bytes, so they are
+      // issued even after an abort, for the drain below to complete.
+      if (ti > x_next) {
+        if constexpr (XPRE) {
+          if (ok) ok = poll_x(ti);
+        } else {
+          poll_x(ti);
+        }
+      }
       if (!ok) *abort_flag = 1;
       // drain: every issued stage's copies must have landed before exit
       const int first = ti > ns ? ti - ns : 0;
@@ -1169,6 +1203,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       unit_range(u, nt, mt, ks0, ks1, sp);
       const int64_t n = (int64_t)nt * kTileN + row;
       if (p.norm_w && !XPRE && mt != norm_mt) {
+        if (p.pdl) pdl_wait();   // the rows are the previous kernel's output
         // RMS factors of the tile's tokens over the full K (every split needs
         // them, so each CTA reads the rows itself, from L2): dequant warp w
         // takes tokens w, w + 16, ...  The previous unit's conversions all
@@ -1766,9 +1801,20 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   ReduceCtx none{};
   const ReduceCtx ctx = rc ? *rc : none;
   const int reduce = rc ? 1 : 0;
+  // programmatic dependent launch (TcParams::pdl): the kernel may start while
+  // the previous kernel on the stream finishes
+  cudaLaunchAttribute pdl_attr;
+  pdl_attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl_attr.val.programmaticStreamSerializationAllowed = 1;
   if (!pl.csplit) {
-    const int grid = std::min(units, sm_count());
-    kern<<<grid, kThreads, pl.smem, s>>>(tw, tx, ts, tz, prm, ctx, reduce);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min(units, sm_count()));
+    cfg.blockDim = dim3((unsigned)kThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = s;
+    cfg.attrs = &pdl_attr;
+    cfg.numAttrs = prm.pdl ? 1 : 0;
+    IE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, tz, prm, ctx, reduce));
     return launch_status("qgemm_tc_kernel");
   }
   // cluster split-K: one cluster of `splits` CTAs per tile in flight, as many
@@ -1779,7 +1825,7 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   cfg.blockDim = dim3((unsigned)kThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)pl.splits;
   attr[0].val.clusterDim.y = 1;
@@ -1800,7 +1846,7 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
       cache_init = true;
     }
     const int dev = current_device();
-    const int key = (int)pl.smem * 16 + pl.splits;
+    const int key = ((int)pl.smem * 16 + pl.splits) * 2 + (pl.xpre ? 1 : 0);
     if (cached_key[dev][FMT] == key) {
       max_clusters = cached_max[dev][FMT];
     } else {
@@ -1815,6 +1861,10 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   TcParams prm2 = prm;
   prm2.nclusters = std::min(tiles, max_clusters);
   cfg.gridDim = dim3((unsigned)(prm2.nclusters * pl.splits));
+  if (prm.pdl) {
+    attr[1] = pdl_attr;
+    cfg.numAttrs = 2;
+  }
   IE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, tz, prm2, ctx, reduce));
   return launch_status("qgemm_tc_kernel");
 }
@@ -1964,6 +2014,9 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
     prm.x = a.x;
     prm.ldx = a.ldx;
   }
+  // Every launch may overlap the previous kernel except one that clears its
+  // tickets first (the memset node sits between the two kernels).
+  prm.pdl = (pl.splits > 1 && !pl.csplit) ? 0 : 1;
   if (pl.xpre) {
     prm.xh = reinterpret_cast<__half*>(ws + pl.xh_off);
     prm.xbar = reinterpret_cast<uint32_t*>(ws);
