@@ -71,6 +71,10 @@ def parse():
                     help="decode batches also timed (the decode_batches field); empty to skip")
     ap.add_argument("--no-dense", action="store_true", help="skip the dense cuBLAS comparator")
     ap.add_argument("--no-parity", action="store_true", help="skip the in-run parity check")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the model-level decode step (attention, lm_head, sampling)")
+    ap.add_argument("--context", type=int, default=2048,
+                    help="tokens already in every sequence's KV cache for the model decode step")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="wall-clock budget of the CPU baseline sample")
     ap.add_argument("--sweep", action="store_true",
@@ -449,6 +453,186 @@ def dense_step(args, world: int, shape, steps: int, warmup: int, nccl, max_over_
 
 
 # ---------------------------------------------------------------------------
+# model-level decode step (decode at a 2048-token context)
+# ---------------------------------------------------------------------------
+MODEL_BLOCK = 256   # KV block size: flash-attn's paged kernels take multiples of 256
+
+
+def _decode_inputs(batch: int, context: int, seed: int):
+    """Static device inputs of one decode step: every sequence holds `context`
+    tokens (positions 0 .. context-2 cached, the new token at context-1) in its
+    own run of KV blocks."""
+    import torch
+
+    per = (context + MODEL_BLOCK - 1) // MODEL_BLOCK
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    tables = torch.arange(batch * per, device="cuda", dtype=torch.long).reshape(batch, per)
+    pos = context - 1
+    return {
+        "tokens": torch.randint(0, 128256, (batch,), generator=gen, device="cuda"),
+        "positions": torch.full((batch,), pos, dtype=torch.long, device="cuda"),
+        "tables": tables,
+        "slots": tables[:, pos // MODEL_BLOCK] * MODEL_BLOCK + pos % MODEL_BLOCK,
+        "context_lens": torch.full((batch,), context, dtype=torch.int32, device="cuda"),
+        "num_blocks": batch * per,
+    }
+
+
+def _graph_ms(step, steps: int, warmup: int, barrier, max_over_ranks):
+    """CUDA-graph one call of `step`, replay it: ms per replay (max over ranks)."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    ms = timed_replays(g.replay, steps, warmup, barrier, max_over_ranks)
+    del g
+    return ms
+
+
+def model_decode(args, rank: int, world: int, comm, nccl, barrier, max_over_ranks) -> dict:
+    """One decode step of the whole Llama-3-8B-shaped model at `args.batch`
+    sequences of `args.context` tokens, through ``QuantizedTransformer.run``
+    (the Engine-protocol model: embedding, per layer qkv / RoPE / KV write /
+    flash-attn paged decode / o + fused all-reduce / gate-up / down + fused
+    all-reduce, final norm) and ``greedy_on_device`` (vocab-parallel lm_head,
+    argmax), with each step's tokens fed back as the next step's input.  The
+    comparator is the same step as the reference's TorchTransformer runs it on
+    the GPU: dense bf16 weights, cuBLAS matmuls, the same RoPE / KV write /
+    flash-attn calls, NCCL all-reduces at N > 1."""
+    import torch
+
+    from ie_tpq.decode import Layout
+    from ie_tpq.model import LLAMA3_8B_CONFIG, QuantizedTransformer, synthetic_source
+    from ie_tpq.sharding import Shard
+
+    cfg = LLAMA3_8B_CONFIG
+    if args.layers != cfg.num_layers:
+        from dataclasses import replace
+
+        cfg = replace(cfg, num_layers=args.layers)
+    batch = args.batch
+    src = synthetic_source(cfg, args.scheme, seed=3)
+    model = QuantizedTransformer(src, scheme=args.scheme, shard=Shard(rank, world),
+                                 comm=comm if world > 1 else None, dtype=torch.bfloat16)
+    del src
+    torch.cuda.empty_cache()
+    inp = _decode_inputs(batch, args.context, seed=11)
+    k_caches, v_caches = model.allocate_caches(inp["num_blocks"], MODEL_BLOCK)
+    plan = {"flash": True, "scale": cfg.head_dim ** -0.5, "slots": inp["slots"],
+            "context_lens": inp["context_lens"], "cu_q": None, "cu_k": None,
+            "paged_tables": None, "tables32": inp["tables"].to(torch.int32)}
+    layout = Layout([0] * batch, [args.context - 1] * batch, [0] * batch,
+                    [args.context] * batch, [1] * batch, [[0]] * batch, False)
+    tokens = inp["tokens"]
+
+    def ours():
+        h = model.run(tokens, inp["positions"], inp["tables"], plan, layout, k_caches,
+                      v_caches, MODEL_BLOCK)
+        tokens.copy_(model.greedy_on_device(h))
+
+    steps = max(20, min(args.steps, 200))
+    ms = _graph_ms(ours, steps, 3, barrier, max_over_ranks)
+    def packed_bytes(w):
+        return (w.codes.numel() + w.scale.numel() * w.scale.element_size() +
+                (w.zero.numel() * w.zero.element_size() if w.zero is not None else 0))
+
+    wbytes = sum(packed_bytes(w) for a, m in zip(model.attn, model.mlp)
+                 for w in ([a.qkv] if a.qkv is not None else [a.q_proj, a.k_proj, a.v_proj]) +
+                 [a.o_proj, m.gate_up, m.down])
+    out = {"tok_s": batch / (ms / 1e3), "ms_per_step": ms, "batch": batch,
+           "context": args.context, "kv_block": MODEL_BLOCK, "steps": steps,
+           "linear_weight_bytes_per_rank": wbytes}
+    del model
+    torch.cuda.empty_cache()
+    if not args.no_dense:
+        dms = _dense_model_ms(args, cfg, world, rank, nccl, inp, k_caches, v_caches, steps,
+                              barrier, max_over_ranks)
+        out["dense_cublas"] = {"tok_s": batch / (dms / 1e3), "ms_per_step": dms,
+                               "speedup_of_ours": dms / ms}
+    del k_caches, v_caches
+    torch.cuda.empty_cache()
+    return out
+
+
+def _dense_model_ms(args, cfg, world, rank, nccl, inp, k_caches, v_caches, steps, barrier,
+                    max_over_ranks) -> float:
+    """The decode step of ``model_decode`` with dense bf16 weights (the
+    reference's TorchTransformer on the GPU: ie/model/torch_transformer.py:31-63,
+    ie/kernels/torch_backend.py:103-127), this rank's TP shards."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from ie_tpq.attention import apply_rope, flash_decode, write_kv
+    from ie_tpq.model import rope_tables_on_device
+
+    h, inter = cfg.hidden_size, cfg.intermediate_size // world
+    hd = cfg.head_dim
+    nh, nkv = cfg.num_heads // world, cfg.num_kv_heads // world
+    vocab = cfg.vocab_size // world
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    mk = lambda n, k: (torch.randn((n, k), generator=gen, device="cuda",
+                                   dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    layers = [{"qkv": mk((nh + 2 * nkv) * hd, h), "o": mk(h, nh * hd), "gu": mk(2 * inter, h),
+               "down": mk(h, inter)} for _ in range(cfg.num_layers)]
+    emb = mk(cfg.vocab_size, h)
+    lm_head = mk(vocab, h)
+    norm = torch.ones(h, dtype=torch.bfloat16, device="cuda")
+    cos, sin = rope_tables_on_device(cfg.max_position, hd, cfg.rope_base, "cuda")
+    tokens = inp["tokens"]
+    scale = hd ** -0.5
+
+    def step():
+        x = emb.index_select(0, tokens)
+        for L, kc, vc in zip(layers, k_caches, v_caches):
+            n = F.rms_norm(x, (h,), norm, cfg.norm_eps)
+            qkv = n @ L["qkv"].t()
+            q = qkv[:, :nh * hd].reshape(-1, nh, hd)
+            k = qkv[:, nh * hd:(nh + nkv) * hd].reshape(-1, nkv, hd)
+            v = qkv[:, (nh + nkv) * hd:].reshape(-1, nkv, hd)
+            q = apply_rope(q, inp["positions"], cos, sin)
+            k = apply_rope(k, inp["positions"], cos, sin)
+            write_kv(k, v, kc, vc, inp["slots"])
+            a = flash_decode(q, kc, vc, inp["tables"].int(), inp["context_lens"], MODEL_BLOCK,
+                             scale).reshape(-1, nh * hd)
+            o_ = a @ L["o"].t()
+            if world > 1:
+                dist.all_reduce(o_, group=nccl)
+            x = x + o_
+            n = F.rms_norm(x, (h,), norm, cfg.norm_eps)
+            gu = n @ L["gu"].t()
+            d = (F.silu(gu[:, :inter]) * gu[:, inter:]) @ L["down"].t()
+            if world > 1:
+                dist.all_reduce(d, group=nccl)
+            x = x + d
+        x = F.rms_norm(x, (h,), norm, cfg.norm_eps)
+        local = (x @ lm_head.t()).float()
+        idx = local.argmax(dim=-1)
+        if world > 1:
+            buf = torch.zeros((world, 2, x.shape[0]), dtype=torch.float32, device="cuda")
+            buf[rank, 0] = local.gather(1, idx[:, None]).squeeze(1)
+            buf[rank, 1] = (idx + rank * vocab).float()
+            dist.all_reduce(buf, group=nccl)
+            idx = buf[:, 1].gather(0, buf[:, 0].argmax(dim=0)[None]).squeeze(0).long()
+        tokens.copy_(idx)
+
+    ms = _graph_ms(step, steps, 3, barrier, max_over_ranks)
+    del layers, emb, lm_head
+    torch.cuda.empty_cache()
+    return ms
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def timed_replays(fn, steps: int, warmup: int, barrier, max_over_ranks):
@@ -619,6 +803,14 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                           "rms_norm/SiLU/residual" + (", NCCL all-reduce" if world > 1 else "") +
                           "; CUDA graph, CUDA events, max over ranks")}
 
+    # ---- the whole model's decode step (attention, lm_head, sampling) --------
+    model = None
+    if not args.no_model:
+        stack = None   # release the linear-path stack (if the dense arm has not)
+        layers.clear()
+        torch.cuda.empty_cache()
+        model = model_decode(args, rank, world, comm, nccl, barrier, max_over_ranks)
+
     if rank == 0:
         base = cpu_reference(args, world)
         line = {
@@ -645,6 +837,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "clocks": clocks,
             "parity": parity,
             "dense_cublas": dense,
+            "model_decode": model,
             "decode_batches": batches,
             "weights_bytes_per_rank": weight_bytes,
         }

@@ -195,6 +195,23 @@ int ie_kernel_status(uint32_t* bits, int32_t clear);
 int ie_rms_norm(const void* x, int64_t ldx, int32_t x_dtype, const float* weight, void* out,
                 int64_t ldo, int32_t out_dtype, int64_t m, int64_t h, float eps, void* stream);
 
+/* ---- rotary embedding + KV-cache write ------------------------------------------
+ * Replaces, for the output of the fused q|k|v projection, the RoPE of q and k
+ * (ie/layers/functional.py:34-61, interleaved or halved) and write_kv
+ * (ie/kernels/torch_backend.py:13-16) with one launch.  qkv [tokens][ld_qkv]
+ * holds q (heads*head_dim), k and v (kv_heads*head_dim each) per row; cos /
+ * sin are f32 [max_position][head_dim/2]; q_out [tokens][heads][head_dim];
+ * the caches [cache_slots][kv_heads][head_dim] receive token t's rotated k and
+ * its v at slots[t].  All activations one dtype (bf16, f16 or f32); each
+ * product and sum is rounded to it, as the unfused elementwise steps do.
+ * Tokens whose slot is outside [0, cache_slots) write no cache row, and
+ * tokens whose position is outside the tables write no rotated q / k. */
+int ie_rope_kv(const void* qkv, int64_t ld_qkv, int32_t dtype, int64_t tokens, int32_t heads,
+               int32_t kv_heads, int32_t head_dim, const int64_t* positions,
+               const float* cos_table, const float* sin_table, int64_t max_position,
+               int32_t halved, const int64_t* slots, void* k_cache, void* v_cache,
+               int64_t cache_slots, void* q_out, void* stream);
+
 /* ---- all_reduce over a list of partials in one process -----------------------
  * Replaces ie/parallel/sharding.py:40-44: out = p[0] + p[1] + ... in rank order
  * (f32 arithmetic, the reference's order).  dtype applies to inputs and out. */

@@ -48,7 +48,7 @@ EXPORTED = (
     "ie_version", "ie_last_error", "ie_quantize_integer", "ie_quantize_float",
     "ie_round_to_float_format", "ie_pack_weight", "ie_dequantize",
     "ie_qlinear_workspace_size", "ie_qlinear", "ie_qlinear_noalloc", "ie_kernel_status",
-    "ie_rms_norm",
+    "ie_rms_norm", "ie_rope_kv",
     "ie_reduce_partials", "ie_comm_create",
     "ie_comm_export", "ie_comm_open", "ie_comm_destroy", "ie_comm_set_timeout",
     "ie_comm_check", "ie_qlinear_allreduce", "ie_allreduce",
@@ -116,6 +116,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "ie_kernel_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _I32]),
         "ie_rms_norm": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _I64, _I32, _I64, _I64,
                                        ctypes.c_float, _P]),
+        "ie_rope_kv": (ctypes.c_int, [_P, _I64, _I32, _I64, _I32, _I32, _I32, _P, _P, _P, _I64,
+                                      _I32, _P, _P, _P, _I64, _P, _P]),
         "ie_reduce_partials": (ctypes.c_int, [ctypes.POINTER(_P), _I32, _P, _I64, _I32, _P]),
         "ie_comm_create": (ctypes.c_int, [_I32, _I32, _I32, ctypes.c_size_t,
                                           ctypes.POINTER(_P)]),

@@ -56,6 +56,35 @@ def apply_rope(x, positions, cos, sin, halved: bool = False):
     return out
 
 
+def rope_write_kv(qkv, heads: int, kv_heads: int, head_dim: int, positions, cos, sin, slots,
+                  k_cache, v_cache, halved: bool = False):
+    """RoPE of q and k and the KV-cache write for the fused q|k|v projection's
+    output ``qkv`` [tokens, (heads + 2 kv_heads) * head_dim] in one launch
+    (``ie_rope_kv``); returns the rotated q [tokens, heads, head_dim].  Bitwise
+    equal to ``apply_rope`` on q and k followed by ``write_kv``."""
+    from . import _lib
+    from .device import dtype_code
+
+    torch = require_cuda()
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("qkv must be a row-contiguous 2-D tensor")
+    if k_cache.dtype != qkv.dtype or v_cache.dtype != qkv.dtype:
+        raise ValueError("the caches must have the activations' dtype")
+    for t, what in ((positions, "positions"), (slots, "slots")):
+        if t.dtype != torch.long or not t.is_contiguous() or t.numel() != qkv.shape[0]:
+            raise ValueError(f"{what} must be a contiguous int64 tensor of one entry per token")
+    if not (cos.dtype == sin.dtype == torch.float32 and cos.is_contiguous()
+            and sin.is_contiguous() and cos.shape[-1] * 2 == head_dim):
+        raise ValueError("cos / sin must be contiguous f32 [max_position, head_dim / 2]")
+    q = torch.empty((qkv.shape[0], heads, head_dim), dtype=qkv.dtype, device=qkv.device)
+    _lib.check(_lib.lib().ie_rope_kv(
+        qkv.data_ptr(), qkv.stride(0), dtype_code(qkv.dtype), qkv.shape[0], heads, kv_heads,
+        head_dim, positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+        1 if halved else 0, slots.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        k_cache.shape[0], q.data_ptr(), _lib.stream_ptr()), "rope_kv")
+    return q
+
+
 def write_kv(k, v, k_cache, v_cache, slots) -> None:
     """ie/kernels/reference.py:42-49 / torch_backend.py:13-16."""
     k_cache.index_copy_(0, slots, k.to(k_cache.dtype))

@@ -18,7 +18,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent                      # inference-engine_b200/
 CSRC = ROOT / "csrc"
 REPO = ROOT.parent
-SOURCES = ["capi.cu", "quant.cu", "gemv.cu", "qgemm_sm100.cu", "comm.cu", "norm.cu"]
+SOURCES = ["capi.cu", "quant.cu", "gemv.cu", "qgemm_sm100.cu", "comm.cu", "norm.cu",
+           "rope_kv.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

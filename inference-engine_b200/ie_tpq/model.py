@@ -31,14 +31,86 @@ the same way, so every rank continues with identical tokens.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
+from types import SimpleNamespace
+
 import numpy as np
 
 from .attention import (FLASH, PAGED_FLASH_BLOCK, allocate_kv_cache, apply_rope, flash_decode,
-                        flash_prefill, paged_attention, write_kv)
+                        flash_prefill, paged_attention, rope_write_kv, write_kv)
 from .device import require_cuda
 from .sharding import Shard
 from .tensor_parallel import (ShardedAttention, ShardedMLP, kv_heads_per_rank, quantized_block,
                               rms_norm)
+
+
+@dataclass
+class DecoderConfig:
+    """The model fields the forward uses (ie/model/transformer.py:12-34)."""
+    vocab_size: int
+    hidden_size: int
+    num_layers: int
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+    intermediate_size: int
+    max_position: int = 4096
+    rope_base: float = 500000.0
+    norm_eps: float = 1e-5
+    rope_halved: bool = False
+
+
+LLAMA3_8B_CONFIG = DecoderConfig(vocab_size=128256, hidden_size=4096, num_layers=32,
+                                 num_heads=32, num_kv_heads=8, head_dim=128,
+                                 intermediate_size=14336)
+
+
+def rope_tables_on_device(max_position: int, head_dim: int, base: float, device):
+    """cos / sin tables (ie/layers/functional.py:20-31) as f32 device tensors."""
+    torch = require_cuda()
+    exps = torch.arange(0, head_dim, 2, dtype=torch.float32, device=device) / head_dim
+    freqs = torch.pow(torch.tensor(base, dtype=torch.float32, device=device), -exps)
+    angles = torch.outer(torch.arange(max_position, dtype=torch.float32, device=device), freqs)
+    return torch.cos(angles), torch.sin(angles)
+
+
+def synthetic_source(config: DecoderConfig, scheme: str, seed: int = 0, std: float = 0.02,
+                     dtype=None, device="cuda"):
+    """A random-init decoder with the reference Transformer's layout (blocks of
+    seven ``[K, N]`` projections, norms, embedding, lm_head, RoPE tables), drawn
+    N(0, std) on the device and quantized there with the reference's tables
+    (``quantize_on_device``): no host copy of the f32 weights, which for a
+    Llama-3-8B shape would be 32 GB.  Norm weights are ones."""
+    torch = require_cuda()
+    from .packed import quantize_on_device
+
+    dtype = dtype or torch.bfloat16
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    h, i = config.hidden_size, config.intermediate_size
+    q_out, kv_out = config.num_heads * config.head_dim, config.num_kv_heads * config.head_dim
+
+    def quant(k, n):
+        w = torch.randn((k, n), generator=gen, device=device, dtype=torch.float32) * std
+        return quantize_on_device(w, scheme)
+
+    blocks = []
+    for _ in range(config.num_layers):
+        blocks.append(SimpleNamespace(
+            config=config, q_proj=quant(h, q_out), k_proj=quant(h, kv_out),
+            v_proj=quant(h, kv_out), o_proj=quant(q_out, h), gate_proj=quant(h, i),
+            up_proj=quant(h, i), down_proj=quant(i, h),
+            attn_norm=torch.ones(h, dtype=torch.float32, device=device),
+            mlp_norm=torch.ones(h, dtype=torch.float32, device=device),
+            q_bias=None, k_bias=None, v_bias=None, q_norm=None, k_norm=None))
+        torch.cuda.empty_cache()
+    rnd = lambda *shape: (torch.randn(shape, generator=gen, device=device,
+                                      dtype=torch.float32) * std).to(dtype)
+    cos, sin = rope_tables_on_device(config.max_position, config.head_dim, config.rope_base,
+                                     device)
+    return SimpleNamespace(config=config, blocks=blocks, embedding=rnd(config.vocab_size, h),
+                           final_norm=torch.ones(h, dtype=torch.float32, device=device),
+                           lm_head=rnd(h, config.vocab_size), cos=cos, sin=sin)
 
 
 class QuantizedTransformer:
@@ -58,8 +130,10 @@ class QuantizedTransformer:
         self.dtype = dtype or torch.float16
         self.scheme = scheme
         kv_heads_per_rank(self.config, self.world)   # raises like the reference
-        take = lambda w, dt=None: torch.from_numpy(np.ascontiguousarray(w)).to(
-            device=self.device, dtype=dt or self.dtype)
+        def take(w, dt=None):
+            t = w if isinstance(w, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(w))
+            return t.to(device=self.device, dtype=dt or self.dtype).contiguous()
+
         self.embedding = take(source.embedding)
         self.attn, self.mlp = [], []
         for block in source.blocks:
@@ -79,6 +153,8 @@ class QuantizedTransformer:
             q = quantize_for_device(np.asarray(source.lm_head, np.float32), scheme, axis)
             self.lm_head_packed = split_output_dim(q, self.shard).packed(self.device)
             self.lm_head = None
+        elif isinstance(source.lm_head, torch.Tensor):
+            self.lm_head = take(source.lm_head[:, cols])
         else:
             self.lm_head = take(np.asarray(source.lm_head)[:, cols])
         self.cos = take(source.cos, torch.float32)
@@ -108,17 +184,29 @@ class QuantizedTransformer:
         from .linear import qlinear
 
         attn, mlp = self.attn[i], self.mlp[i]
-        q, k, v = attn.project_qkv(x)
-        q = apply_rope(q, positions, self.cos, self.sin, attn.rope_halved)
-        k = apply_rope(k, positions, self.cos, self.sin, attn.rope_halved)
-        write_kv(k, v, k_cache, v_cache, plan["slots"])
+        # A prefill of fresh prompts attends over its own k and v (not the
+        # cache) and needs them as tensors; every other step reads the cache.
+        needs_kv = plan["flash"] and layout.is_prefill and plan["paged_tables"] is None
+        qkv = None if needs_kv else attn.fused_qkv(x)
+        if qkv is not None:   # RoPE of q and k and the cache write in one launch
+            q = rope_write_kv(qkv, attn.num_heads, attn.num_kv_heads, self.config.head_dim,
+                              positions, self.cos, self.sin, plan["slots"], k_cache, v_cache,
+                              attn.rope_halved)
+            k = v = None
+        else:
+            q, k, v = attn.project_qkv(x)
+            q = apply_rope(q, positions, self.cos, self.sin, attn.rope_halved)
+            k = apply_rope(k, positions, self.cos, self.sin, attn.rope_halved)
+            write_kv(k, v, k_cache, v_cache, plan["slots"])
         if plan["flash"]:
             if layout.is_prefill:
                 attended = flash_prefill(q, k, v, k_cache, v_cache, plan["cu_q"], plan["cu_k"],
                                          layout.max_query_len, layout.max_context_len,
                                          plan["paged_tables"], block_size, plan["scale"])
             else:
-                attended = flash_decode(q, k_cache, v_cache, block_tables.int(),
+                tables = plan.get("tables32")
+                attended = flash_decode(q, k_cache, v_cache,
+                                        tables if tables is not None else block_tables.int(),
                                         plan["context_lens"], block_size, plan["scale"])
         else:
             attended = paged_attention(q, k_cache, v_cache, block_tables, layout.context_lens,
@@ -169,6 +257,8 @@ class QuantizedTransformer:
             "paged_tables": (block_tables.to(torch.int32)
                              if use_flash and layout.max_context_len > layout.max_query_len
                              else None),
+            "tables32": (block_tables.to(torch.int32)
+                         if use_flash and not layout.is_prefill else None),
         }
         return self.run(tokens, positions, block_tables, plan, layout, k_caches, v_caches,
                         block_size)
@@ -190,6 +280,32 @@ class QuantizedTransformer:
                            device=self.device)
         full[:, self.vocab_slice] = local
         return self.comm.all_reduce(full)
+
+    def greedy_on_device(self, hidden) -> "torch.Tensor":
+        """Argmax token of every row of ``hidden`` as a device tensor, without
+        gathering full-vocabulary logits: each rank takes the first maximum of
+        its vocabulary slice, and the ranks' (value, index) pairs are summed
+        into a zeroed [world, 2, rows] buffer (a concatenation); the first
+        rank holding the largest value wins, which is the first maximum of
+        the full row (torch_transformer.py:131-140 at temperature 0)."""
+        torch = require_cuda()
+        if self.lm_head_packed is not None:
+            from .linear import qlinear
+
+            local = qlinear(hidden.contiguous(), self.lm_head_packed, out_dtype=torch.float32)
+        else:
+            local = (hidden @ self.lm_head).float()
+        idx = local.argmax(dim=-1)
+        if self.world == 1:
+            return idx
+        val = local.gather(1, idx[:, None]).squeeze(1)
+        buf = torch.zeros((self.world, 2, hidden.shape[0]), dtype=torch.float32,
+                          device=self.device)
+        buf[self.shard.rank, 0] = val
+        buf[self.shard.rank, 1] = (idx + self.vocab_slice.start).float()
+        both = self.comm.all_reduce(buf)
+        best = both[:, 0].argmax(dim=0)
+        return both[:, 1].gather(0, best[None]).squeeze(0).long()
 
     def logits_for_last_token_of_each(self, hidden, query_lens) -> np.ndarray:
         return self.logits_on_device(hidden, query_lens).float().cpu().numpy()

@@ -157,27 +157,40 @@ class ShardedAttention:
         self.q_bias = bias(getattr(block, "q_bias", None), config.num_heads)
         self.k_bias = bias(getattr(block, "k_bias", None), config.num_kv_heads)
         self.v_bias = bias(getattr(block, "v_bias", None), config.num_kv_heads)
+        # the fused projection's bias, q|k|v in row order (None without biases)
+        self.qkv_bias = (torch.cat([self.q_bias, self.k_bias, self.v_bias]).contiguous()
+                         if self.q_bias is not None else None)
         self.q_norm = _f32(getattr(block, "q_norm", None), self.device)
         self.k_norm = _f32(getattr(block, "k_norm", None), self.device)
         self.rope_halved = bool(getattr(config, "rope_halved", False))
 
+    def _norm_in(self, x, first):
+        from .linear import fuse_norm_pays
+
+        if fuse_norm_pays(x, first):
+            return x, self.norm
+        return rms_norm(x, self.norm, self.eps), None
+
+    def fused_qkv(self, x):
+        """The q|k|v projection as one GEMM output ``[T, (heads + 2 kv_heads) * hd]``
+        when the rank's q, k and v share one packed weight and no per-head
+        q / k norm follows (the input of ``rope_write_kv``); else None."""
+        from .linear import qlinear
+
+        if self.qkv is None or self.q_norm is not None:
+            return None
+        h, nw = self._norm_in(x, self.qkv)
+        return qlinear(h, self.qkv, bias=self.qkv_bias, norm_weight=nw, norm_eps=self.eps)
+
     def project_qkv(self, x):
         """q, k, v ``[T, heads, hd]`` of this rank for hidden states x (device)."""
-        from .linear import fuse_norm_pays, qlinear
+        from .linear import qlinear
 
-        torch = require_cuda()
         hd = self.config.head_dim
-        first = self.qkv if self.qkv is not None else self.q_proj
-        if fuse_norm_pays(x, first):
-            h, nw = x, self.norm
-        else:
-            h, nw = rms_norm(x, self.norm, self.eps), None
+        h, nw = self._norm_in(x, self.qkv if self.qkv is not None else self.q_proj)
         qn, kn = self.num_heads * hd, self.num_kv_heads * hd
         if self.qkv is not None:
-            bias = None
-            if self.q_bias is not None:
-                bias = torch.cat([self.q_bias, self.k_bias, self.v_bias])
-            y = qlinear(h, self.qkv, bias=bias, norm_weight=nw, norm_eps=self.eps)
+            y = qlinear(h, self.qkv, bias=self.qkv_bias, norm_weight=nw, norm_eps=self.eps)
             q, k, v = y[:, :qn], y[:, qn:qn + kn], y[:, qn + kn:]
         else:
             q = qlinear(h, self.q_proj, bias=self.q_bias, norm_weight=nw, norm_eps=self.eps)
