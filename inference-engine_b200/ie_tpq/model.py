@@ -147,11 +147,19 @@ class QuantizedTransformer:
         self.vocab_slice = cols
         self.lm_head_packed = None
         if quantize_lm_head:
-            from .quant_model import quantize_for_device
             from .sharding import split_output_dim
 
-            q = quantize_for_device(np.asarray(source.lm_head, np.float32), scheme, axis)
-            self.lm_head_packed = split_output_dim(q, self.shard).packed(self.device)
+            if isinstance(source.lm_head, torch.Tensor):
+                from .packed import quantize_on_device
+
+                q = quantize_on_device(source.lm_head.to(self.device, torch.float32).contiguous(),
+                                       scheme, axis)
+                self.lm_head_packed = split_output_dim(q, self.shard)
+            else:
+                from .quant_model import quantize_for_device
+
+                q = quantize_for_device(np.asarray(source.lm_head, np.float32), scheme, axis)
+                self.lm_head_packed = split_output_dim(q, self.shard).packed(self.device)
             self.lm_head = None
         elif isinstance(source.lm_head, torch.Tensor):
             self.lm_head = take(source.lm_head[:, cols])

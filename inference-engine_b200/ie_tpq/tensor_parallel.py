@@ -76,6 +76,18 @@ def _pack(w, device=None) -> PackedWeight:
     raise TypeError("expected a QuantizedWeight or PackedWeight")
 
 
+def _own(p: PackedWeight) -> PackedWeight:
+    """A column shard that does not keep the whole weight alive: a row slice
+    of packed codes is a view of the full array, so it is copied out."""
+    base = p.codes._base
+    if base is None or base.numel() == p.codes.numel():
+        return p
+    return PackedWeight(fmt=p.fmt, axis=p.axis, k=p.k, n=p.n, codes=p.codes.clone(),
+                        scale=p.scale.clone(), zero=p.zero.clone() if p.zero is not None else None,
+                        int4_symmetric=p.int4_symmetric, gate_up=p.gate_up,
+                        unrepresentable=p.unrepresentable)
+
+
 def _f32(v, device):
     """A host vector (or None) as a contiguous f32 device tensor."""
     if v is None:
@@ -138,9 +150,9 @@ class ShardedAttention:
         self.num_kv_heads = config.num_kv_heads // shard.world_size
         self.norm = _f32(block.attn_norm, self.device)
         self.eps = float(config.norm_eps)
-        q = _pack(split_heads(block.q_proj, shard, config.num_heads, hd), self.device)
-        k = _pack(split_heads(block.k_proj, shard, config.num_kv_heads, hd), self.device)
-        v = _pack(split_heads(block.v_proj, shard, config.num_kv_heads, hd), self.device)
+        q = _own(_pack(split_heads(block.q_proj, shard, config.num_heads, hd), self.device))
+        k = _own(_pack(split_heads(block.k_proj, shard, config.num_kv_heads, hd), self.device))
+        v = _own(_pack(split_heads(block.v_proj, shard, config.num_kv_heads, hd), self.device))
         self.q_proj, self.k_proj, self.v_proj = q, k, v
         # one GEMM for q|k|v when their tables live on N (per-N, group-128)
         self.qkv = concat_rows([q, k, v]) if q.axis in (_lib.IE_AXIS_N, _lib.IE_AXIS_GROUP128) \
