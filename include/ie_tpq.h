@@ -28,7 +28,8 @@
 extern "C" {
 #endif
 
-#define IE_TPQ_ABI_VERSION 2   /* 2: ie_qlinear_args gained norm_weight / norm_eps */
+#define IE_TPQ_ABI_VERSION 3   /* 2: ie_qlinear_args gained norm_weight / norm_eps;
+                                  3: its last field became act_quant */
 
 /* ---- status codes --------------------------------------------------- */
 #define IE_OK 0
@@ -103,8 +104,20 @@ typedef struct ie_qlinear_args {
   size_t workspace_bytes;
   const float* norm_weight;  /* IE_EPI_RMS_NORM: f32 [k], 16-byte aligned */
   float norm_eps;
-  int32_t reserved;
+  int32_t act_quant;    /* IE_ACT_* (0: the activations as given) */
 } ie_qlinear_args;
+
+/* Activation quantization (ie_qlinear_args.act_quant).  IE_ACT_FP8_TOKEN: each
+ * token row of x is quantized to e4m3 with its own scale, the reference's
+ * quantize_float(x, FP8_E4M3, axis=0) (ie/quant/weights.py:73-81, scale
+ * max|x_t| / 448, codes by round_to_float_format), and the e4m3 codes of x and
+ * of an FP8 weight are contracted directly by the tensor cores
+ * (tcgen05.mma kind::f8f6f4, f32 accumulators); the epilogue multiplies by the
+ * token's scale and the weight's per-N or per-tensor scale.  FP8 weights with
+ * IE_AXIS_N or IE_AXIS_TENSOR scales, bf16/f16 x, the tensor-core path and a
+ * workspace (ie_qlinear_workspace_size) only; else IE_ERR_INVALID. */
+#define IE_ACT_NONE 0
+#define IE_ACT_FP8_TOKEN 1
 
 /* ---- library ------------------------------------------------------------ */
 int ie_version(void);

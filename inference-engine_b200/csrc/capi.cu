@@ -55,6 +55,19 @@ int validate_linear(const ie_qlinear_args& a) {
     IE_CHECK(a.algo != 1, "qlinear: the fused RMS norm runs on the tensor-core path only");
   }
   IE_CHECK(a.algo >= 0 && a.algo <= 2, "qlinear: unknown algo %d", a.algo);
+  IE_CHECK(a.act_quant == IE_ACT_NONE || a.act_quant == IE_ACT_FP8_TOKEN,
+           "qlinear: unknown act_quant %d", a.act_quant);
+  if (a.act_quant == IE_ACT_FP8_TOKEN) {
+    IE_CHECK(a.w.format == IE_FMT_FP8_E4M3 &&
+                 (a.w.axis == IE_AXIS_N || a.w.axis == IE_AXIS_TENSOR),
+             "qlinear: fp8 activations need an FP8 weight with per-N or per-tensor scales "
+             "(per-K scales vary along the contraction)");
+    IE_CHECK(a.act_dtype == IE_DT_BF16 || a.act_dtype == IE_DT_F16,
+             "qlinear: fp8 activations are quantized from bf16/f16 x");
+    IE_CHECK(a.algo != 1 && !(a.epilogue & IE_EPI_RMS_NORM),
+             "qlinear: fp8 activations run on the tensor-core path, without the fused norm");
+    IE_CHECK(a.w.k % 128 == 0, "qlinear: fp8 activations need K %% 128 == 0");
+  }
   return IE_OK;
 }
 

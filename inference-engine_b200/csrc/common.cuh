@@ -42,6 +42,33 @@ inline int launch_status(const char* what) {
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ---- element conversion ------------------------------------------------------
+// ---------------------------------------------------------------------------
+// round_to_float_format (ie/quant/formats.py:74-79)
+// ---------------------------------------------------------------------------
+// The reference clips to +-max, takes frexp's mantissa m in [0.5, 1), rounds
+// m * 2^mb half-to-even and rescales: the value keeps mb significant bits.
+// Rounding an IEEE float to its top `sig` significant bits is an integer add
+// on its bit pattern: add just under half an ulp of the kept field plus the
+// kept field's lowest bit (ties to even), then clear the dropped bits; a
+// carry out of the mantissa correctly bumps the exponent.
+struct FloatFmt {
+  int mantissa_bits;
+  float max_value;
+  float flush_below;  // min_normal * 2^-mantissa_bits
+};
+
+__device__ __forceinline__ float round_to_format(float x, FloatFmt f) {
+  x = fminf(fmaxf(x, -f.max_value), f.max_value);
+  const int drop = 23 - (f.mantissa_bits - 1);
+  uint32_t u = __float_as_uint(x);
+  const uint32_t lsb = (u >> drop) & 1u;
+  u += ((1u << (drop - 1)) - 1u) + lsb;
+  u &= ~((1u << drop) - 1u);
+  float out = __uint_as_float(u);
+  out = fminf(fmaxf(out, -f.max_value), f.max_value);
+  return fabsf(out) < f.flush_below ? 0.0f : out;
+}
+
 template <typename T> __device__ __forceinline__ float to_f32(T v);
 template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
 template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {

@@ -69,7 +69,10 @@ constexpr int kMaxAStages = 6;
 constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 2 GHz
 constexpr int kMinSmem = 120 * 1024;              // keeps one CTA per SM
 
-enum Fmt { F_INT4G = 0, F_INT4SYM = 1, F_INT8 = 2, F_FP8 = 3 };
+// F_FP8N: fp8 weights contracted natively with per-token fp8 activations
+// (IE_ACT_FP8_TOKEN): no dequantization, A read by the MMA from shared memory.
+enum Fmt { F_INT4G = 0, F_INT4SYM = 1, F_INT8 = 2, F_FP8 = 3, F_FP8N = 4 };
+constexpr int kFmts = 5;
 
 // error bits recorded by kernels of this file (read with ie_kernel_status)
 __device__ uint32_t g_tc_status = 0;
@@ -119,8 +122,9 @@ struct TcParams {
   // advances; waiters wait for it to leave the value read at kernel start.
   // Every CTA arrives exactly once (at teardown if it gave up before), so
   // the words are consistent for the next launch without being cleared.
-  __half* xh;
+  __half* xh;               // F_FP8N: the e4m3 codes of x, [M][K] bytes
   uint32_t* xbar;
+  float* xs;                // F_FP8N: per-token activation scales [M]
   // Launched as a programmatic dependent of the previous kernel on the stream:
   // the prologue and the first weight stages overlap that kernel's tail, and
   // nothing it writes (x, the residual, RMS-norm rows, the all-reduce epoch,
@@ -325,6 +329,16 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem], e4m3 x e4m3 (K = 32 per instruction)
+__device__ __forceinline__ void tc_mma_ss_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // The loaded registers are defined only once tcgen05.wait::ld returns, so the
 // load and the wait form one asm statement (no use can be scheduled between).
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
@@ -406,8 +420,8 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return sw128_desc_from(sw128_desc_lo(saddr));
 }
 
-// Instruction descriptor: kind::f16, f32 accumulator, f16 A and B, both
-// K-major, M = 128, N = n.
+// Instruction descriptor: f32 accumulator, A and B type 0 (f16 for kind::f16,
+// e4m3 for kind::f8f6f4), both K-major, M = 128, N = n.
 __host__ __device__ constexpr uint32_t make_idesc(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTileN >> 4) << 24);
 }
@@ -758,6 +772,65 @@ __device__ __forceinline__ bool xpre_slice(const TcParams& p, int dt, int warp_i
   return true;
 }
 
+// Per-token e4m3 activations (IE_ACT_FP8_TOKEN), the reference's
+// quantize_float(x, FP8_E4M3, axis=0) (ie/quant/weights.py:73-81): scale
+// max|x_t| / 448 (1 for an all-zero row), codes round_to_float_format(x / s)
+// (ie/quant/formats.py:74-79), stored as e4m3 bytes.  One warp per token row,
+// the rows strided over every dequant warp of the grid; the max is exact in
+// any order and every division is the IEEE f32 one, so the codes and scales
+// equal the reference's (a code below e4m3's normal range that keeps more
+// fraction bits than an e4m3 subnormal becomes the nearest e4m3 value).
+__device__ __forceinline__ void fp8_act_rows(const TcParams& p, int warp_i, int lane) {
+  const FloatFmt e4m3{3, 448.0f, 0.001953125f};   // max 448, flush below 2^-6 * 2^-3
+  const int64_t cpr = p.K / 8;
+  const int64_t nw = (int64_t)gridDim.x * kDqWarps;
+  uint8_t* xq = reinterpret_cast<uint8_t*>(p.xh);
+  bool wrote = false;
+  for (int64_t t = (int64_t)blockIdx.x * kDqWarps + warp_i; t < p.M; t += nw) {
+    const uint4* row = reinterpret_cast<const uint4*>(static_cast<const char*>(p.x) +
+                                                       t * p.ldx * 2);
+    auto widen = [&](const uint4& v, float (&f)[8]) {
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (p.x_bf16) {
+          f[2 * i] = __uint_as_float(u[i] << 16);
+          f[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+        } else {
+          const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+          f[2 * i] = h.x;
+          f[2 * i + 1] = h.y;
+        }
+      }
+    };
+    float amax = 0.0f;
+    for (int64_t c = lane; c < cpr; c += 32) {
+      float f[8];
+      widen(__ldcg(row + c), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 448.0f);
+    if (lane == 0) p.xs[t] = sc;
+    for (int64_t c = lane; c < cpr; c += 32) {
+      float f[8];
+      widen(__ldcg(row + c), f);
+      uint32_t b[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float code = round_to_format(__fdiv_rn(f[i], sc), e4m3);
+        const uint32_t byte = (uint32_t)__nv_cvt_float_to_fp8(code, __NV_SATFINITE, __NV_E4M3);
+        b[i >> 2] |= byte << (8 * (i & 3));
+      }
+      *reinterpret_cast<uint2*>(xq + t * p.K + c * 8) = make_uint2(b[0], b[1]);
+      wrote = true;
+    }
+  }
+  if (wrote) fence_proxy_async_all();   // these stores, before other CTAs' TMA reads
+}
+
 // Epilogue value of token m, row n, before the residual: scale, then bias.
 struct Epi {
   const TcParams& p;
@@ -849,10 +922,13 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   // the compiler still knows every derived pointer is shared memory (a round
   // trip through an integer would turn their accesses into generic ones)
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr bool NATIVE = FMT == F_FP8N;
+  static_assert(!NATIVE || XPRE, "fp8 activations are made by the pre-pass");
   const int ns = p.ns, na = p.na, sub = p.sub;
   // one TMA stage = `sub` consecutive 128-K sub-stages behind one full/empty pair
   const int w_sub_bytes = p.w_stage_bytes / sub;           // [128 rows][row bytes] per sub
-  const int x_sub_bytes = p.bn * kBK * 2;                    // two SW128 blocks per sub
+  // f16 x: two SW128 blocks per sub-stage; e4m3 x (NATIVE): one
+  const int x_sub_bytes = p.bn * kBK * (NATIVE ? 1 : 2);
   const int x_stage_bytes = x_sub_bytes * sub;
   uint8_t* x_ring = smem;                                   // ns x x_stage_bytes
   uint8_t* w_ring = x_ring + ns * x_stage_bytes;            // ns x w_stage_bytes
@@ -895,7 +971,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], p.issuers + kDqWarps);   // each issuer's commit + every dequant warp
+      // each issuer's commit + every dequant warp (NATIVE: the issuers only)
+      mbar_init(&empty[s], p.issuers + (NATIVE ? 0 : kDqWarps));
       mbar_init(&xfull[s], 1);
     }
     for (int s = 0; s < na; ++s) {
@@ -978,9 +1055,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       auto issue_x = [&](int tj, int mt, int ks) {
         const int sj = tj % ns;
         // every 64-wide K block of the stage's activation tile in one copy
-        if constexpr (XPRE) {
+        if constexpr (XPRE) {   // (K blocks of 64 f16, or NATIVE of 128 e4m3 bytes)
           mbar_expect_tx(&xfull[sj], (uint32_t)x_stage_bytes);
-          tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &xfull[sj]);
+          tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, NATIVE ? ks : ks * 2,
+                      &xfull[sj]);
         } else {   // the stage's full barrier already expects these bytes
           tma_load_3d(x_ring + sj * x_stage_bytes, &tm_x, 0, mt * p.bn, ks * 2, &full[sj]);
         }
@@ -1117,10 +1195,29 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             ok = false;
             break;
           }
+          if constexpr (NATIVE) {   // the stage's weight tile is the A operand as it landed
+            if (!mbar_wait(&full[s], s_ph, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
           // this issuer's sub-stages of the stage, j = first, first + issuers, ...;
           // sub-stage j uses A slot (a + j) mod na
           const int first = p.issuers == 1 ? 0 : (issuer ^ (lsub & 1));
-          for (int j = first; j < nsub; j += p.issuers) {
+          for (int j = first; j < nsub && NATIVE; j += p.issuers) {
+            // e4m3 weights [128 rows][128 K] and x [bn][128 K], both one SW128
+            // block: four K = 32 steps of 32 bytes
+            const uint32_t w_lo =
+                sw128_desc_lo(smem_u32(w_ring + s * p.w_stage_bytes + j * w_sub_bytes));
+            const uint32_t xb = x_lo + (uint32_t)j * x_sub16;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 32; ++kk)
+              tc_mma_ss_f8(dcol[kk], sw128_desc_from(w_lo + (uint32_t)(kk * 2)),
+                           sw128_desc_from(xb + (uint32_t)(kk * 2)), idesc, (mask >> kk) & 1u);
+            mask = 0xFFu;
+          }
+          for (int j = first; j < nsub && !NATIVE; j += p.issuers) {
             uint32_t aj = a + (uint32_t)j, phj = a_ph;
             while (aj >= (uint32_t)na) {
               aj -= (uint32_t)na;
@@ -1143,10 +1240,12 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           }
           if (!ok) break;
           lsub += nsub;
-          a += (uint32_t)nsub;
-          while (a >= (uint32_t)na) {
-            a -= (uint32_t)na;
-            a_ph ^= 1u;
+          if constexpr (!NATIVE) {   // (NATIVE has no A ring)
+            a += (uint32_t)nsub;
+            while (a >= (uint32_t)na) {
+              a -= (uint32_t)na;
+              a_ph ^= 1u;
+            }
           }
           tc_commit(&empty[s]);
           if (++s == (uint32_t)ns) {
@@ -1192,11 +1291,22 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       // need no activations); the producer waits before loading x tiles.
       const int64_t total = p.M * (p.K / 8);
       const int64_t g = gridDim.x, b = blockIdx.x;
-      ok = xpre_slice(p, dt, warp - kDqWarp0, lane, s_rinv, total * b / g, total * (b + 1) / g,
-                      dq_sync);
+      if constexpr (NATIVE)
+        fp8_act_rows(p, warp - kDqWarp0, lane);
+      else
+        ok = xpre_slice(p, dt, warp - kDqWarp0, lane, s_rinv, total * b / g,
+                        total * (b + 1) / g, dq_sync);
       if (ok) ok = dq_sync();
       if (ok && dt == 0) xbar_arrive();
     }
+    // NATIVE: the accumulators are sums of e4m3 code products; token t's values
+    // take its activation scale after the weight's (nscale)
+    auto token_scales = [&](int64_t m0c, float (&v)[8]) {
+      if constexpr (NATIVE) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] *= (m0c + j < p.M) ? p.xs[m0c + j] : 0.0f;
+      }
+    };
     int norm_mt = -1;   // token tile whose RMS factors s_rinv holds
     for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
       int nt, mt, ks0, ks1, sp;
@@ -1225,7 +1335,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
       int lsub = 0;   // sub-stage index within the unit; pair lsub % kPairs takes it
-      for (int ks = ks0; ks < ks1 && ok; ks += sub) {
+      // (NATIVE: nothing to dequantize, the MMAs read the stages themselves)
+      for (int ks = ks0; ks < ks1 && ok && !NATIVE; ks += sub) {
         const int nsub = min(sub, ks1 - ks);
         // wait for this use of the stage even without a sub-stage to dequantize:
         // the arrival on empty[s] below must not run ahead of the producer
@@ -1377,6 +1488,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         if (!split) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[j] *= nscale;
+          token_scales(m0 + c0, v);
           epi.emit8(m0 + c0, n, v, lane);
         }
       }
@@ -1415,6 +1527,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[j] *= nscale;
+            token_scales(m0 + c0, acc);
             epi.emit8(m0 + c0, n, acc, lane);
           }
           // hand the receive buffer back to every other split of the cluster
@@ -1467,6 +1580,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             }
         #pragma unroll
             for (int jj = 0; jj < 8; ++jj) acc[jj] *= nscale;
+            token_scales(m0 + c0, acc);
             epi.emit8(m0 + c0, n, acc, lane, res);
           }
           if (dt == 0) p.counters[tile_id] = 0u;
@@ -1601,7 +1715,8 @@ struct Plan {
   size_t ws_bytes = 0;       // counters + pre-pass activations + partials
   size_t counters_off = 0;   // split-K tile tickets, cleared by every launch that uses them
   size_t counters_bytes = 0;
-  size_t xh_off = 0;         // pre-pass activations xh [M][K] f16
+  size_t xh_off = 0;         // pre-pass activations xh [M][K] f16 (F_FP8N: e4m3 bytes)
+  size_t xs_off = 0;         // F_FP8N: per-token activation scales [M] f32
   size_t part_off = 0;       // split-K partials [splits][M][N] f32
   bool csplit = false;       // splits of a tile as one thread-block cluster
   bool xpre = false;         // activation pre-pass (bf16 or RMS-norm activations)
@@ -1641,7 +1756,9 @@ int fmt_of(const ie_qweight& w) {
 // plus the f32 partials' extra traffic spread over the SMs.
 Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
   Plan pl;
-  pl.fmt = fmt_of(a.w);
+  pl.fmt = a.act_quant == IE_ACT_FP8_TOKEN ? F_FP8N : fmt_of(a.w);
+  const bool native = pl.fmt == F_FP8N;
+  const int xe = native ? 1 : 2;   // bytes of one x element in the MMA's B operand
   const int64_t M = a.m;
   pl.bn = (int)std::min<int64_t>(256, ((M + 15) / 16) * 16);
   pl.m_tiles = (int)((M + pl.bn - 1) / pl.bn);
@@ -1660,13 +1777,13 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
     const bool norm = (a.epilogue & IE_EPI_RMS_NORM) != 0;
     const double per_sm = (double)pl.n_tiles * (double)M * (double)a.w.k / sm_count();
     const bool pays = norm ? M > 16 : per_sm >= 256.0 * 1024.0;
-    pl.xpre = allow_xpre && (a.act_dtype == IE_DT_BF16 || norm) && pays;
+    pl.xpre = allow_xpre && (native || ((a.act_dtype == IE_DT_BF16 || norm) && pays));
   }
   const int row_stage = (pl.fmt == F_INT4G || pl.fmt == F_INT4SYM) ? kBK / 2 : kBK;
   // a TMA stage carries 32 KB of weights (4 int4 groups or 2 8-bit ones) when the
   // token tile leaves room: large stages amortise the barrier round trips
   pl.sub = row_stage == kBK / 2 ? 4 : 2;
-  while (pl.sub > 1 && (size_t)pl.sub * (row_stage * kTileN + pl.bn * kBK * 2) > 100 * 1024)
+  while (pl.sub > 1 && (size_t)pl.sub * (row_stage * kTileN + pl.bn * kBK * xe) > 100 * 1024)
     pl.sub /= 2;
   pl.w_stage_bytes = row_stage * kTileN * pl.sub;
   const int sms = sm_count();
@@ -1726,15 +1843,17 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
   // (Two chains for tiles up to 64 tokens: four were no faster in the mainloop
   // and cost the epilogue a second TMEM round trip for the extra accumulators.)
   pl.chains = pl.bn <= 64 ? 2 : 1;
-  pl.issuers = (2 * pl.acc_cols * pl.chains + 4 * kACols <= 512) ? 2 : 1;
+  pl.issuers = (2 * pl.acc_cols * pl.chains + (native ? 0 : 4 * kACols) <= 512) ? 2 : 1;
   const int accs = pl.acc_cols * pl.chains * pl.issuers;
   // The A ring covers a sub-stage's dequant plus its MMAs' latency (8 MMAs take
-  // ~0.45 us from issue to commit), so it is as deep as TMEM allows.
-  pl.na = accs + kMaxAStages * kACols <= 512 ? kMaxAStages
-                                             : (accs + 4 * kACols <= 512 ? 4 : 2);
+  // ~0.45 us from issue to commit), so it is as deep as TMEM allows.  F_FP8N
+  // reads A from shared memory and has none.
+  pl.na = native ? 0
+                 : (accs + kMaxAStages * kACols <= 512 ? kMaxAStages
+                                                       : (accs + 4 * kACols <= 512 ? 4 : 2));
   pl.tmem_cols = 32;
   while (pl.tmem_cols < accs + pl.na * kACols) pl.tmem_cols *= 2;
-  const size_t x_stage = (size_t)pl.bn * kBK * 2 * pl.sub;
+  const size_t x_stage = (size_t)pl.bn * kBK * xe * pl.sub;
   // Small token tiles: the splits of a tile run as one cluster and reduce
   // through the leader's shared memory (receive buffer); no workspace.
   if (pl.splits > 1 && best_cluster) {
@@ -1758,8 +1877,10 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
   pl.counters_off = 256;
   pl.counters_bytes = global_split ? ((size_t)tiles * 4 + 255) / 256 * 256 : 0;
   pl.xh_off = pl.counters_off + pl.counters_bytes;
-  const size_t xh_bytes = pl.xpre ? ((size_t)M * a.w.k * 2 + 255) / 256 * 256 : 0;
-  pl.part_off = pl.xh_off + xh_bytes;
+  const size_t xh_bytes = pl.xpre ? ((size_t)M * a.w.k * xe + 255) / 256 * 256 : 0;
+  pl.xs_off = pl.xh_off + xh_bytes;
+  const size_t xs_bytes = native ? ((size_t)M * 4 + 255) / 256 * 256 : 0;
+  pl.part_off = pl.xs_off + xs_bytes;
   const size_t part_bytes = global_split ? (size_t)pl.splits * M * a.w.n * 4 : 0;
   pl.ws_bytes = (global_split || pl.xpre) ? pl.part_off + part_bytes : 0;
   return pl;
@@ -1791,10 +1912,16 @@ template <int FMT>
 int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw,
                  const CUtensorMap& tx, const CUtensorMap& ts, const CUtensorMap& tz,
                  const TcParams& prm, const ReduceCtx* rc, cudaStream_t s) {
-  auto kern = pl.csplit ? (pl.xpre ? qgemm_tc_kernel<FMT, true, true>
-                                    : qgemm_tc_kernel<FMT, true, false>)
-                        : (pl.xpre ? qgemm_tc_kernel<FMT, false, true>
-                                   : qgemm_tc_kernel<FMT, false, false>);
+  // (F_FP8N always has the pre-pass: it makes the e4m3 activations)
+  decltype(&qgemm_tc_kernel<FMT, false, true>) kern;
+  if constexpr (FMT == F_FP8N) {
+    kern = pl.csplit ? qgemm_tc_kernel<FMT, true, true> : qgemm_tc_kernel<FMT, false, true>;
+  } else {
+    kern = pl.csplit ? (pl.xpre ? qgemm_tc_kernel<FMT, true, true>
+                                : qgemm_tc_kernel<FMT, true, false>)
+                     : (pl.xpre ? qgemm_tc_kernel<FMT, false, true>
+                                : qgemm_tc_kernel<FMT, false, false>);
+  }
   IE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)pl.smem));
   const int units = pl.n_tiles * pl.m_tiles * pl.splits;
@@ -1835,7 +1962,7 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   cfg.gridDim = dim3((unsigned)(tiles * pl.splits));
   // occupancy of one (shared memory, cluster size) configuration, per device
   static std::mutex mu;
-  static int cached_key[kMaxDevOrdinals][4], cached_max[kMaxDevOrdinals][4];
+  static int cached_key[kMaxDevOrdinals][kFmts], cached_max[kMaxDevOrdinals][kFmts];
   static bool cache_init = false;
   int max_clusters = 0;
   {
@@ -1889,6 +2016,14 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
                            "== 0, 16-byte aligned rows (and norm weight) and the driver's TMA "
                            "encoder");
   const Plan pl = fitting_plan(a, a.workspace ? a.workspace_bytes : 0);
+  if (pl.fmt == F_FP8N && !pl.xpre)
+    return set_error(IE_ERR_INVALID, "qlinear: fp8 activations need a workspace of %zu bytes "
+                                     "(ie_qlinear_workspace_size); %zu given",
+                     make_plan(a, false, true).ws_bytes, a.workspace ? a.workspace_bytes : 0);
+  // the pre-pass producer remembers a stage's x coordinates in 16 bits each
+  IE_CHECK(!pl.xpre || (pl.m_tiles < 65536 && pl.kstages < 65536),
+           "qlinear: %d token tiles / %d K stages exceed the pre-pass limits", pl.m_tiles,
+           pl.kstages);
   EncodeFn enc = encode_fn();
   CUtensorMap tw, tx;
   {
@@ -1911,12 +2046,17 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   {
     // x viewed as [K/64][M][64]: one box {64, BN, 2} is a stage's two SW128 blocks;
     // with the pre-pass the tiles come from xh (f16, rows of K)
+    // (F_FP8N: e4m3 codes [K/128][M][128 bytes], one block {128, BN, sub} a stage)
+    const bool native = pl.fmt == F_FP8N;
     const int64_t ld = pl.xpre ? a.w.k : a.ldx;
-    const cuuint64_t dims[3] = {64, (cuuint64_t)a.m, (cuuint64_t)(a.w.k / 64)};
-    const cuuint64_t strides[2] = {(cuuint64_t)ld * 2, 128};
-    const cuuint32_t box[3] = {64, (cuuint32_t)pl.bn, (cuuint32_t)(2 * pl.sub)};
+    const cuuint64_t inner = native ? 128 : 64;
+    const cuuint64_t dims[3] = {inner, (cuuint64_t)a.m, (cuuint64_t)(a.w.k / inner)};
+    const cuuint64_t strides[2] = {(cuuint64_t)ld * (native ? 1 : 2), 128};
+    const cuuint32_t box[3] = {(cuuint32_t)inner, (cuuint32_t)pl.bn,
+                               (cuuint32_t)((native ? 1 : 2) * pl.sub)};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUtensorMapDataType dt = (a.act_dtype == IE_DT_BF16 && !pl.xpre)
+    const CUtensorMapDataType dt = native ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : (a.act_dtype == IE_DT_BF16 && !pl.xpre)
                                        ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     void* base = pl.xpre ? static_cast<void*>(ws + pl.xh_off) : const_cast<void*>(a.x);
@@ -2020,11 +2160,13 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   if (pl.xpre) {
     prm.xh = reinterpret_cast<__half*>(ws + pl.xh_off);
     prm.xbar = reinterpret_cast<uint32_t*>(ws);
+    if (pl.fmt == F_FP8N) prm.xs = reinterpret_cast<float*>(ws + pl.xs_off);
   }
   switch (pl.fmt) {
     case F_INT4G: return launch_typed<F_INT4G>(a, pl, tw, tx, ts, tz, prm, rc, s);
     case F_INT4SYM: return launch_typed<F_INT4SYM>(a, pl, tw, tx, ts, tz, prm, rc, s);
     case F_INT8: return launch_typed<F_INT8>(a, pl, tw, tx, ts, tz, prm, rc, s);
+    case F_FP8N: return launch_typed<F_FP8N>(a, pl, tw, tx, ts, tz, prm, rc, s);
     default: return launch_typed<F_FP8>(a, pl, tw, tx, ts, tz, prm, rc, s);
   }
 }

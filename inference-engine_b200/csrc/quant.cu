@@ -16,33 +16,8 @@ namespace {
 
 constexpr int kThreads = 256;
 
-// ---------------------------------------------------------------------------
-// round_to_float_format (ie/quant/formats.py:74-79)
-// ---------------------------------------------------------------------------
-// The reference clips to +-max, takes frexp's mantissa m in [0.5, 1), rounds
-// m * 2^mb half-to-even and rescales: the value keeps mb significant bits.
-// Rounding an IEEE float to its top `sig` significant bits is an integer add
-// on its bit pattern: add just under half an ulp of the kept field plus the
-// kept field's lowest bit (ties to even), then clear the dropped bits; a
-// carry out of the mantissa correctly bumps the exponent.
-struct FloatFmt {
-  int mantissa_bits;
-  float max_value;
-  float flush_below;  // min_normal * 2^-mantissa_bits
-};
-
-__device__ __forceinline__ float round_to_format(float x, FloatFmt f) {
-  x = fminf(fmaxf(x, -f.max_value), f.max_value);
-  const int drop = 23 - (f.mantissa_bits - 1);
-  uint32_t u = __float_as_uint(x);
-  const uint32_t lsb = (u >> drop) & 1u;
-  u += ((1u << (drop - 1)) - 1u) + lsb;
-  u &= ~((1u << drop) - 1u);
-  float out = __uint_as_float(u);
-  out = fminf(fmaxf(out, -f.max_value), f.max_value);
-  return fabsf(out) < f.flush_below ? 0.0f : out;
-}
-
+// round_to_float_format (ie/quant/formats.py:74-79): round_to_format and
+// FloatFmt in common.cuh.
 FloatFmt make_float_fmt(int e, int m, int reserves_inf) {
   const int bias = (1 << (e - 1)) - 1;
   double largest, mscale;

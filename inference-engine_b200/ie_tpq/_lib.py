@@ -39,6 +39,7 @@ IE_EPI_BIAS = 1
 IE_EPI_RESIDUAL = 2
 IE_EPI_SILU_MUL = 4
 IE_EPI_RMS_NORM = 8
+IE_ACT_NONE, IE_ACT_FP8_TOKEN = 0, 1
 
 IE_COMM_HANDLE_BYTES = 64
 IE_QLINEAR_NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -88,7 +89,7 @@ class QLinearArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("norm_weight", ctypes.c_void_p),
         ("norm_eps", ctypes.c_float),
-        ("reserved", ctypes.c_int32),
+        ("act_quant", ctypes.c_int32),
     ]
 
 

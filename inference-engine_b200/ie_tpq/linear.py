@@ -58,7 +58,7 @@ def fuse_norm_pays(x, w: PackedWeight) -> bool:
 
 def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=False,
                algo=ALGO_AUTO, workspace=None, norm_weight=None,
-               norm_eps: float = 1e-6) -> _lib.QLinearArgs:
+               norm_eps: float = 1e-6, act_quant: int = 0) -> _lib.QLinearArgs:
     if x.dim() != 2:
         raise ValueError(f"x must be 2-D [tokens, K], got shape {tuple(x.shape)}")
     if x.shape[1] != w.k:
@@ -94,6 +94,7 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
     a.epilogue = epi
     a.norm_weight = norm_weight.data_ptr() if norm_weight is not None else None
     a.norm_eps = float(norm_eps)
+    a.act_quant = int(act_quant)
     a.algo = algo
     a.workspace = workspace.data_ptr() if workspace is not None else None
     a.workspace_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
@@ -102,7 +103,7 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
 
 def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | None = None,
             out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None,
-            workspace=None, norm_weight=None, norm_eps: float = 1e-6):
+            workspace=None, norm_weight=None, norm_eps: float = 1e-6, act_quant: int = 0):
     """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce.
 
     x: CUDA tensor ``[M, K]`` (bf16 / f16 / f32).  bias: f32 ``[N]``.  residual:
@@ -110,7 +111,9 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
     weight returns ``silu(gate) * up`` of shape ``[M, N/2]``.  ``norm_weight``
     (f32 ``[K]``) folds ``rms_norm(x, norm_weight, norm_eps)`` in front of the
     product (ie/layers/functional.py:6-8); it needs the tensor-core path
-    (``fused_norm_ok``) and raises otherwise.
+    (``fused_norm_ok``) and raises otherwise.  ``act_quant=IE_ACT_FP8_TOKEN``
+    (fp8 weights with per-N or per-tensor scales) quantizes each token of x to
+    e4m3 with its own scale and contracts the e4m3 codes on the tensor cores.
     """
     torch = require_cuda()
     if silu_mul is None:
@@ -125,7 +128,7 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
                                     or not norm_weight.is_contiguous()):
         norm_weight = norm_weight.to(torch.float32).contiguous()
     a = build_args(x, w, out, bias=bias, residual=residual, silu_mul=silu_mul, algo=algo,
-                   norm_weight=norm_weight, norm_eps=norm_eps)
+                   norm_weight=norm_weight, norm_eps=norm_eps, act_quant=act_quant)
     need = _lib.lib().ie_qlinear_workspace_size(ctypes.byref(a))
     if need:
         ws = workspace if workspace is not None else shared_workspace(need, x.device)

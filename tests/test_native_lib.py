@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.ie_version() == 2
+    assert lib.ie_version() == 3
 
 
 def test_invalid_arguments_are_rejected_before_any_cuda_call():
