@@ -81,7 +81,7 @@ def parse():
                     help="the isolated row-parallel GEMM + all-reduce sweep (one JSON line per "
                          "case) instead of the decode step")
     ap.add_argument("--sweep-m", default="1,8,64,512,4096,16384")
-    ap.add_argument("--sweep-formats", default="int8,int4-g128,fp8")
+    ap.add_argument("--sweep-formats", default="int8,int4-g128,fp8,fp8-native")
     return ap.parse_args()
 
 
@@ -862,16 +862,25 @@ NVLINK_GBS = 770.0   # measured B200 peer copy bandwidth, GB/s per direction
 def sweep_bounds(scheme: str, m: int, k: int, n: int, world: int, w_bytes: float,
                  peaks: dict) -> dict:
     """Lower bounds of one rank's fused launch: HBM bytes (packed weights, x,
-    out), tensor FLOPs and one-shot NVLink bytes ((world - 1) bf16 partials)."""
+    out), tensor FLOPs and one-shot NVLink bytes ((world - 1) bf16 partials).
+    The tensor bound is the measured bf16 GEMM rate, or twice it for the
+    native fp8 contraction (B200's dense fp8 rate is twice its bf16 rate)."""
     hbm = w_bytes + m * k * 2 + m * n * 2
     flops = 2.0 * m * k * n
     nvl = (world - 1) * m * n * 2
+    tensor_peak = peaks["bf16_tflops"] * (2.0 if scheme == "fp8-native" else 1.0)
     t = {"hbm": hbm / (peaks["hbm_gbs"] * 1e9),
-         "tensor": flops / (peaks["bf16_tflops"] * 1e12),
+         "tensor": flops / (tensor_peak * 1e12),
          "nvlink": nvl / (NVLINK_GBS * 1e9)}
     bound = max(t, key=t.get)
     return {"bound": bound, "t_min_us": t[bound] * 1e6, "hbm_bytes": hbm, "flops": flops,
             "nvlink_bytes": nvl}
+
+
+def _lib_act_fp8() -> int:
+    from ie_tpq import _lib
+
+    return _lib.IE_ACT_FP8_TOKEN
 
 
 def run_sweep(args, rank: int, world: int, local: int) -> None:
@@ -943,7 +952,12 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
             gen.manual_seed(0)
             full = torch.randn((kk, n), generator=gen, device="cuda") * 0.02
             k = kk // world
-            w = quantize_on_device(full, scheme).slice_k(rank * k, (rank + 1) * k)
+            # fp8-native: per-N fp8 weights and per-token fp8 activations on
+            # the tensor cores (act_quant); the others dequantize the weight
+            native = scheme == "fp8-native"
+            act = _lib_act_fp8() if native else 0
+            w = quantize_on_device(full, "fp8" if native else scheme,
+                                   axis=1 if native else 0).slice_k(rank * k, (rank + 1) * k)
             del full
             # the dense comparator keeps the dequantized bf16 shard resident
             w_dense = w.dequantize("nk", torch.bfloat16)
@@ -954,7 +968,7 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
                 out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
 
                 def fused():
-                    qlinear(x, w, out=out, comm=comm)
+                    qlinear(x, w, out=out, comm=comm, act_quant=act)
 
                 def unfused():
                     wd = w.dequantize("nk", torch.bfloat16)

@@ -772,63 +772,99 @@ __device__ __forceinline__ bool xpre_slice(const TcParams& p, int dt, int warp_i
   return true;
 }
 
+// Largest |x| of one K-long row by one warp (exact in any order).
+__device__ __forceinline__ float row_amax(const void* row, int64_t K, int x_bf16, int lane) {
+  float mx = 0.0f;
+  const uint4* r = static_cast<const uint4*>(row);
+  const int64_t chunks = K / 8;
+  for (int64_t c0 = lane; c0 < chunks; c0 += 32 * kSumsqLoads) {
+    uint4 v[kSumsqLoads];
+#pragma unroll
+    for (int j = 0; j < kSumsqLoads; ++j)
+      v[j] = c0 + 32 * j < chunks ? __ldcg(r + c0 + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < kSumsqLoads; ++j) {
+      const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (x_bf16) {   // |bf16| as the top half of an f32 with the sign cleared
+          mx = fmaxf(mx, __uint_as_float((u[i] << 16) & 0x7FFFFFFFu));
+          mx = fmaxf(mx, __uint_as_float(u[i] & 0x7FFF0000u));
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+          mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  return mx;
+}
+
 // Per-token e4m3 activations (IE_ACT_FP8_TOKEN), the reference's
 // quantize_float(x, FP8_E4M3, axis=0) (ie/quant/weights.py:73-81): scale
 // max|x_t| / 448 (1 for an all-zero row), codes round_to_float_format(x / s)
-// (ie/quant/formats.py:74-79), stored as e4m3 bytes.  One warp per token row,
-// the rows strided over every dequant warp of the grid; the max is exact in
-// any order and every division is the IEEE f32 one, so the codes and scales
-// equal the reference's (a code below e4m3's normal range that keeps more
-// fraction bits than an e4m3 subnormal becomes the nearest e4m3 value).
-__device__ __forceinline__ void fp8_act_rows(const TcParams& p, int warp_i, int lane) {
+// (ie/quant/formats.py:74-79), stored as e4m3 bytes.  Each CTA takes the same
+// share of all M*K/8 chunks as the bf16 pre-pass (xpre_slice): per round of
+// up to kDqWarps tokens its warps take one token's row maximum each (every
+// CTA that touches a token computes the same value, the one holding the
+// token's first chunk stores its scale), then all threads quantize the
+// round's chunks.  The maximum is exact in any order and the divisions are
+// IEEE f32, so codes and scales equal the reference's (a code below e4m3's
+// normal range that keeps more fraction bits than an e4m3 subnormal becomes
+// the nearest e4m3 value).
+template <class Sync>
+__device__ __forceinline__ bool fp8_act_slice(const TcParams& p, int dt, int warp_i, int lane,
+                                              float* s_sc, int64_t c0, int64_t c1,
+                                              const Sync& dq_sync) {
   const FloatFmt e4m3{3, 448.0f, 0.001953125f};   // max 448, flush below 2^-6 * 2^-3
   const int64_t cpr = p.K / 8;
-  const int64_t nw = (int64_t)gridDim.x * kDqWarps;
+  const uint4* x = static_cast<const uint4*>(p.x);
   uint8_t* xq = reinterpret_cast<uint8_t*>(p.xh);
+  const int64_t rs = p.ldx / 8;
+  if (c1 <= c0) return true;
+  const int64_t t_first = c0 / cpr, t_last = (c1 - 1) / cpr;
   bool wrote = false;
-  for (int64_t t = (int64_t)blockIdx.x * kDqWarps + warp_i; t < p.M; t += nw) {
-    const uint4* row = reinterpret_cast<const uint4*>(static_cast<const char*>(p.x) +
-                                                       t * p.ldx * 2);
-    auto widen = [&](const uint4& v, float (&f)[8]) {
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (p.x_bf16) {
-          f[2 * i] = __uint_as_float(u[i] << 16);
-          f[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
-        } else {
-          const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
-          f[2 * i] = h.x;
-          f[2 * i + 1] = h.y;
-        }
+  for (int64_t t0 = t_first; t0 <= t_last; t0 += kDqWarps) {
+    const int64_t t1 = t_last + 1 < t0 + kDqWarps ? t_last + 1 : t0 + kDqWarps;
+    for (int64_t t = t0 + warp_i; t < t1; t += kDqWarps) {
+      const float amax = row_amax(static_cast<const char*>(p.x) + t * p.ldx * 2, p.K,
+                                  p.x_bf16, lane);
+      const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 448.0f);
+      if (lane == 0) {
+        s_sc[t - t0] = sc;
+        if (t * cpr >= c0) p.xs[t] = sc;
       }
-    };
-    float amax = 0.0f;
-    for (int64_t c = lane; c < cpr; c += 32) {
-      float f[8];
-      widen(__ldcg(row + c), f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
     }
+    if (!dq_sync()) return false;
+    const int64_t a = c0 > t0 * cpr ? c0 : t0 * cpr, b = c1 < t1 * cpr ? c1 : t1 * cpr;
+    for (int64_t i = a + dt; i < b; i += kDqThreads) {
+      const int64_t t = i / cpr, kc = i - t * cpr;
+      const uint4 v = __ldcg(x + t * rs + kc);
+      const float sc = s_sc[t - t0];
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      uint32_t bytes[2] = {0u, 0u};
 #pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 448.0f);
-    if (lane == 0) p.xs[t] = sc;
-    for (int64_t c = lane; c < cpr; c += 32) {
-      float f[8];
-      widen(__ldcg(row + c), f);
-      uint32_t b[2] = {0u, 0u};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float code = round_to_format(__fdiv_rn(f[i], sc), e4m3);
+      for (int e = 0; e < 8; ++e) {
+        float f;
+        if (p.x_bf16) {
+          f = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+        } else {
+          const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&u[e >> 1]));
+          f = (e & 1) ? h.y : h.x;
+        }
+        const float code = round_to_format(__fdiv_rn(f, sc), e4m3);
         const uint32_t byte = (uint32_t)__nv_cvt_float_to_fp8(code, __NV_SATFINITE, __NV_E4M3);
-        b[i >> 2] |= byte << (8 * (i & 3));
+        bytes[e >> 2] |= byte << (8 * (e & 3));
       }
-      *reinterpret_cast<uint2*>(xq + t * p.K + c * 8) = make_uint2(b[0], b[1]);
+      *reinterpret_cast<uint2*>(xq + t * p.K + kc * 8) = make_uint2(bytes[0], bytes[1]);
       wrote = true;
     }
+    if (!dq_sync()) return false;   // s_sc is rewritten next round
   }
   if (wrote) fence_proxy_async_all();   // these stores, before other CTAs' TMA reads
+  return true;
 }
 
 // Epilogue value of token m, row n, before the residual: scale, then bias.
@@ -1292,7 +1328,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const int64_t total = p.M * (p.K / 8);
       const int64_t g = gridDim.x, b = blockIdx.x;
       if constexpr (NATIVE)
-        fp8_act_rows(p, warp - kDqWarp0, lane);
+        ok = fp8_act_slice(p, dt, warp - kDqWarp0, lane, s_rinv, total * b / g,
+                           total * (b + 1) / g, dq_sync);
       else
         ok = xpre_slice(p, dt, warp - kDqWarp0, lane, s_rinv, total * b / g,
                         total * (b + 1) / g, dq_sync);
