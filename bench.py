@@ -56,6 +56,23 @@ UNIT = "tok/s"
 RTOL, ATOL = 2e-2, 2e-3
 
 
+# name -> (linear-path shape in ie_tpq.stack, model config in ie_tpq.model)
+MODELS = {"llama3-8b": ("LLAMA3_8B", "LLAMA3_8B_CONFIG"),
+          "llama3-70b": ("LLAMA3_70B", "LLAMA3_70B_CONFIG")}
+
+
+def model_shape(args):
+    import ie_tpq.stack as st
+
+    return getattr(st, MODELS[args.model][0])
+
+
+def model_config(args):
+    import ie_tpq.model as md
+
+    return getattr(md, MODELS[args.model][1])
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -63,7 +80,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=16)
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--model", choices=sorted(MODELS), default="llama3-8b",
+                    help="decoder shape: Llama-3-8B (BASELINE config 3) or Llama-3-70B (config 4)")
+    ap.add_argument("--layers", type=int, default=None, help="default: the model's")
     ap.add_argument("--scheme", default="int4-g128")
     ap.add_argument("--unfused-norm", action="store_true",
                     help="run each rms_norm as its own kernel instead of inside the next GEMM")
@@ -82,7 +101,10 @@ def parse():
                          "case) instead of the decode step")
     ap.add_argument("--sweep-m", default="1,8,64,512,4096,16384")
     ap.add_argument("--sweep-formats", default="int8,int4-g128,fp8,fp8-native")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.layers is None:
+        args.layers = {"llama3-8b": 32, "llama3-70b": 80}[args.model]
+    return args
 
 
 def dist_env():
@@ -160,7 +182,9 @@ def cpu_reference(args, world: int, steps: int | None = None, warmup: int = 1) -
     from oracle import tpq_oracle as o
 
     cores = os.cpu_count() or 1
-    shape = dict(hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=14336)
+    ms = model_shape(args)
+    shape = dict(hidden=ms.hidden, heads=ms.heads, kv_heads=ms.kv_heads, head_dim=ms.head_dim,
+                 inter=ms.intermediate)
     h, i = shape["hidden"], shape["inter"]
     q_out, kv_out = shape["heads"] * shape["head_dim"], shape["kv_heads"] * shape["head_dim"]
     rng = np.random.default_rng(0)
@@ -207,7 +231,7 @@ def cpu_reference(args, world: int, steps: int | None = None, warmup: int = 1) -
     step = per_layer * args.layers
     return {"value": args.batch / step, "unit": UNIT, "cores": cores, "threads": threads,
             "kind": "port", "layers_timed": reps, "extrapolated_from_layers": 1,
-            "sample": (f"{reps} passes over 1 of {args.layers} layers (Llama-3-8B shapes, "
+            "sample": (f"{reps} passes over 1 of {args.layers} layers ({args.model} shapes, "
                        f"batch {args.batch}, TP={world} ranks in sequence), NumPy f32 on "
                        f"dequantized weights with {threads} BLAS threads on {cores} cores, "
                        f"scaled x{args.layers} to the step"),
@@ -241,8 +265,8 @@ def measured_traffic(args, kern_bytes: float, shape) -> tuple:
     capture of the same kernel at TP=1, batch 16, int4-g128, scaled to this
     rank's launch by its algorithmic bytes (the traffic grows with the weight
     rows a rank owns).  None when the workload differs from the capture's."""
-    if args.scheme != "int4-g128" or args.batch != 16:
-        return None, "no capture for this scheme/batch"
+    if args.scheme != "int4-g128" or args.batch != 16 or args.model != "llama3-8b":
+        return None, "no capture for this model/scheme/batch"
     try:
         text = PROFILE.read_text()
     except OSError:
@@ -260,10 +284,13 @@ def measured_traffic(args, kern_bytes: float, shape) -> tuple:
 
 
 def workload_config(args, world: int) -> dict:
-    return {"workload": (f"Llama-3-8B-shaped decoder, quantized linear path of one decode step "
+    name = {"llama3-8b": "Llama-3-8B", "llama3-70b": "Llama-3-70B"}[args.model]
+    acts = ("bf16 activations quantized per token to e4m3" if args.scheme == "fp8-native"
+            else "bf16 activations")
+    return {"workload": (f"{name}-shaped decoder, quantized linear path of one decode step "
                          f"({args.layers} layers: qkv, o+allreduce, gate/up+SiLU, "
-                         f"down+allreduce), {args.scheme} weights, bf16 activations"),
-            "model": "llama3-8b-shaped (random init)", "scheme": args.scheme,
+                         f"down+allreduce), {args.scheme} weights, {acts}"),
+            "model": f"{args.model}-shaped (random init)", "scheme": args.scheme,
             "global_batch": args.batch, "seq_len": 1, "layers": args.layers,
             "parallelism": f"tp{world}",
             "l2": "weights per rank exceed the 126 MB L2; no flush between steps"}
@@ -288,28 +315,40 @@ def parity_check(args, rank: int, world: int, shape, layer, seed: int, dist) -> 
     import numpy as np
     import torch
 
-    from ie_tpq.linear import qlinear
+    from ie_tpq.linear import fused_norm_ok, qlinear
     from ie_tpq.tensor_parallel import rms_norm
     from oracle import tpq_oracle as o
 
     h, inter = shape.hidden, shape.intermediate
     q_cols = shape.q_out // world
+    native = args.scheme == "fp8-native"
     gen = torch.Generator(device="cuda")
     gen.manual_seed(4242)
     x = torch.randn((args.batch, h), generator=gen, device="cuda").to(torch.bfloat16)
     norm = torch.ones(h, dtype=torch.float32, device="cuda")
     comm = layer.get("_comm")
+
+    def norm_in(v, w):
+        """(GEMM input, folded norm weight): the norm folded into the GEMM, or
+        applied first (weights whose activations are quantized per token)."""
+        return (v, norm) if fused_norm_ok(v, w) else (rms_norm(v, norm), None)
+
+    first = layer["qkv"] if "qkv" in layer else layer["q"]
+    h0, nw0 = norm_in(x, first)
     if "qkv" in layer:
-        qkv = qlinear(x, layer["qkv"], norm_weight=norm)
+        qkv = qlinear(h0, layer["qkv"], norm_weight=nw0)
     else:
-        qkv = torch.cat([qlinear(x, layer[n], norm_weight=norm) for n in ("q", "k", "v")], 1)
+        qkv = torch.cat([qlinear(h0, layer[n], norm_weight=nw0) for n in ("q", "k", "v")], 1)
     a = qkv[:, :q_cols].contiguous()
     x1 = qlinear(a, layer["o"], residual=x, comm=comm if world > 1 else None)
-    u = qlinear(x1, layer["gate_up"], norm_weight=norm)
+    h1, nw1 = norm_in(x1, layer["gate_up"])
+    u = qlinear(h1, layer["gate_up"], norm_weight=nw1)
     x2 = qlinear(u, layer["down"], residual=x1, comm=comm if world > 1 else None)
     torch.cuda.synchronize()
     host = {k: v.float().cpu().numpy() for k, v in
-            (("x", x), ("qkv", qkv), ("a", a), ("x1", x1), ("u", u), ("x2", x2))}
+            (("x", x), ("h0", h0), ("h1", h1), ("qkv", qkv), ("a", a), ("x1", x1), ("u", u),
+             ("x2", x2))}
+    fused0, fused1 = nw0 is not None, nw1 is not None
     if world > 1:
         gathered = [None] * world
         dist.all_gather_object(gathered, host)
@@ -329,11 +368,29 @@ def parity_check(args, rank: int, world: int, shape, layer, seed: int, dist) -> 
         full[name] = torch.randn((k, n), generator=g2, device="cuda", dtype=torch.float32) * 0.02
     rng = np.random.default_rng(99)
 
-    def deq_cols(w, cols):
+    def deq_cols(w, cols, rows=None):
+        """The oracle's dequantized weight on a subset of output columns (and
+        a row shard): group-128 and per-N tables are per output column."""
         sub = w[:, torch.as_tensor(cols, device="cuda")].cpu().numpy()
         if args.scheme == "int4-g128":
-            return o.quantize_int4_group128(sub).dequantized()
-        raise ValueError("parity check implemented for int4-g128")
+            out = o.quantize_int4_group128(sub).dequantized()
+        elif native:
+            out = o.quantize_float(sub, *o.E4M3, axis=1).dequantized()
+        else:
+            raise ValueError("parity check implemented for int4-g128 and fp8-native")
+        return out if rows is None else out[rows]
+
+    def act(v):
+        """A GEMM's activations as the kernel contracts them: per-token e4m3
+        for fp8-native (o.quantize_activations_fp8), else as given."""
+        return o.quantize_activations_fp8(v).dequantized() if native else v
+
+    def row_parallel(parts, w, cols):
+        """sum over ranks of act(x_r) @ W[rows of r] -- each rank quantizes its
+        own K slice per token."""
+        k = w.shape[0] // world
+        wd = deq_cols(w, cols)
+        return sum(act(xr) @ wd[r * k:(r + 1) * k] for r, xr in enumerate(parts))
 
     report, ok, worst = {}, bitwise, 0.0
 
@@ -348,29 +405,35 @@ def parity_check(args, rank: int, world: int, shape, layer, seed: int, dist) -> 
     heads = shape.heads
     hd = shape.head_dim
     xs = gathered[0]["x"]
-    n0 = o.rms_norm(xs, np.ones(h, np.float32))
+    # the GEMM inputs: the oracle's rms_norm where the kernel folds it in, else
+    # the normalised activations the GPU computed and fed to the GEMM
+    n0 = act(o.rms_norm(xs, np.ones(h, np.float32)) if fused0 else gathered[0]["h0"])
     # qkv: rank r holds heads [r H/w, (r+1) H/w) of q, k and v
     q_all = np.concatenate([g["qkv"][:, :q_cols] for g in gathered], axis=1)
     cols = np.sort(rng.choice(shape.q_out, size=min(PARITY_COLS, shape.q_out), replace=False))
     compare("qkv(q heads)", q_all[:, cols], n0 @ deq_cols(full["q"], cols))
     # o: x1 = x + sum_r a_r @ Wo[rows of r]
-    a_all = np.concatenate([g["a"] for g in gathered], axis=1)
     cols = np.sort(rng.choice(h, size=PARITY_COLS, replace=False))
     compare("o+allreduce+residual", gathered[0]["x1"][:, cols],
-            xs[:, cols] + a_all @ deq_cols(full["o"], cols))
+            xs[:, cols] + row_parallel([g["a"] for g in gathered], full["o"], cols))
     # gate/up: rank r holds columns [r I/w, (r+1) I/w) of both
-    n1 = o.rms_norm(gathered[0]["x1"], np.ones(h, np.float32))
+    n1 = act(o.rms_norm(gathered[0]["x1"], np.ones(h, np.float32)) if fused1
+             else gathered[0]["h1"])
     u_all = np.concatenate([g["u"] for g in gathered], axis=1)
     cols = np.sort(rng.choice(inter, size=PARITY_COLS, replace=False))
     want = o.silu(n1 @ deq_cols(full["gate"], cols)) * (n1 @ deq_cols(full["up"], cols))
     compare("gate/up+silu", u_all[:, cols], want)
     cols = np.sort(rng.choice(h, size=PARITY_COLS, replace=False))
     compare("down+allreduce+residual", gathered[0]["x2"][:, cols],
-            gathered[0]["x1"][:, cols] + u_all @ deq_cols(full["down"], cols))
+            gathered[0]["x1"][:, cols] + row_parallel([g["u"] for g in gathered], full["down"],
+                                                      cols))
     del full
     torch.cuda.empty_cache()
     return {"ok": ok, "max_abs": worst, "ranks_bitwise_equal": bitwise, "rtol": RTOL,
-            "atol": ATOL, "oracle": "oracle/tpq_oracle.py int4 group-128, f32 dequant-matmul",
+            "atol": ATOL,
+            "oracle": ("oracle/tpq_oracle.py " +
+                       ("per-token e4m3 activations (quantize_activations_fp8) and per-N e4m3 "
+                        "weights" if native else "int4 group-128") + ", f32 dequant-matmul"),
             "shapes": {"qkv": [h, (shape.q_out + 2 * shape.kv_out) // world],
                        "o": [shape.q_out // world, h], "gate_up": [h, 2 * inter // world],
                        "down": [inter // world, h]},
@@ -511,10 +574,10 @@ def model_decode(args, rank: int, world: int, comm, nccl, barrier, max_over_rank
     import torch
 
     from ie_tpq.decode import Layout
-    from ie_tpq.model import LLAMA3_8B_CONFIG, QuantizedTransformer, synthetic_source
+    from ie_tpq.model import QuantizedTransformer, synthetic_source
     from ie_tpq.sharding import Shard
 
-    cfg = LLAMA3_8B_CONFIG
+    cfg = model_config(args)
     if args.layers != cfg.num_layers:
         from dataclasses import replace
 
@@ -668,9 +731,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     from ie_tpq.comm import Communicator
     from ie_tpq.linear import qlinear
     from ie_tpq.sharding import Shard
-    from ie_tpq.stack import LLAMA3_8B, LinearStack, layer_weight_bytes, synthetic_layer
+    from ie_tpq.stack import LinearStack, layer_weight_bytes, synthetic_layer
 
-    shape = LLAMA3_8B
+    shape = model_shape(args)
     shard = Shard(rank, world)
     comm = None
     if world > 1:
@@ -821,7 +884,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_source": traffic_src,
-                         "kernel": "qgemm_tc_kernel (tcgen05) gate/up, int4-g128, fused SiLU*up",
+                         "kernel": f"qgemm_tc_kernel (tcgen05) gate/up, {args.scheme}, fused SiLU*up",
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
                          "algorithmic_bytes_per_launch": kern_bytes,
                          "launch_us": kern_ms * 1e3,

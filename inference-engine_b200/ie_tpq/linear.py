@@ -45,9 +45,11 @@ FUSED_NORM_MAX_TOKENS = 16
 
 def fused_norm_ok(x, w: PackedWeight) -> bool:
     """Whether ``qlinear(x, w, norm_weight=...)`` can fold the RMS norm in:
-    the tensor-core path (bf16/f16 rows, 16-byte aligned, K a multiple of 128)."""
+    the tensor-core path (bf16/f16 rows, 16-byte aligned, K a multiple of 128)
+    with the activations contracted as given (not quantized per token)."""
     torch = require_cuda()
     return (x.dim() == 2 and x.dtype in (torch.bfloat16, torch.float16) and w.k % 128 == 0
+            and not w.act_quant
             and x.stride(1) == 1 and x.data_ptr() % 16 == 0 and (x.stride(0) * 2) % 16 == 0)
 
 
@@ -103,7 +105,8 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
 
 def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | None = None,
             out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None,
-            workspace=None, norm_weight=None, norm_eps: float = 1e-6, act_quant: int = 0):
+            workspace=None, norm_weight=None, norm_eps: float = 1e-6,
+            act_quant: int | None = None):
     """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce.
 
     x: CUDA tensor ``[M, K]`` (bf16 / f16 / f32).  bias: f32 ``[N]``.  residual:
@@ -118,6 +121,8 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
     torch = require_cuda()
     if silu_mul is None:
         silu_mul = w.gate_up
+    if act_quant is None:   # the weight's scheme decides ("fp8-native": per-token e4m3)
+        act_quant = w.act_quant
     out_dtype = out_dtype or x.dtype
     cols = w.out_features if silu_mul else w.n
     if out is None:

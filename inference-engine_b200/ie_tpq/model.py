@@ -63,6 +63,9 @@ class DecoderConfig:
 LLAMA3_8B_CONFIG = DecoderConfig(vocab_size=128256, hidden_size=4096, num_layers=32,
                                  num_heads=32, num_kv_heads=8, head_dim=128,
                                  intermediate_size=14336)
+LLAMA3_70B_CONFIG = DecoderConfig(vocab_size=128256, hidden_size=8192, num_layers=80,
+                                  num_heads=64, num_kv_heads=8, head_dim=128,
+                                  intermediate_size=28672, max_position=8192)
 
 
 def rope_tables_on_device(max_position: int, head_dim: int, base: float, device):
@@ -80,7 +83,9 @@ def synthetic_source(config: DecoderConfig, scheme: str, seed: int = 0, std: flo
     seven ``[K, N]`` projections, norms, embedding, lm_head, RoPE tables), drawn
     N(0, std) on the device and quantized there with the reference's tables
     (``quantize_on_device``): no host copy of the f32 weights, which for a
-    Llama-3-8B shape would be 32 GB.  Norm weights are ones."""
+    Llama-3-8B shape would be 32 GB.  ``blocks`` yields one block at a time, so
+    a tensor-parallel rank holds one full block plus its shards.  Norm weights
+    are ones."""
     torch = require_cuda()
     from .packed import quantize_on_device
 
@@ -94,21 +99,22 @@ def synthetic_source(config: DecoderConfig, scheme: str, seed: int = 0, std: flo
         w = torch.randn((k, n), generator=gen, device=device, dtype=torch.float32) * std
         return quantize_on_device(w, scheme)
 
-    blocks = []
-    for _ in range(config.num_layers):
-        blocks.append(SimpleNamespace(
-            config=config, q_proj=quant(h, q_out), k_proj=quant(h, kv_out),
-            v_proj=quant(h, kv_out), o_proj=quant(q_out, h), gate_proj=quant(h, i),
-            up_proj=quant(h, i), down_proj=quant(i, h),
-            attn_norm=torch.ones(h, dtype=torch.float32, device=device),
-            mlp_norm=torch.ones(h, dtype=torch.float32, device=device),
-            q_bias=None, k_bias=None, v_bias=None, q_norm=None, k_norm=None))
-        torch.cuda.empty_cache()
+    def blocks():   # one block at a time: a consumer keeps only its shards
+        for _ in range(config.num_layers):
+            yield SimpleNamespace(
+                config=config, q_proj=quant(h, q_out), k_proj=quant(h, kv_out),
+                v_proj=quant(h, kv_out), o_proj=quant(q_out, h), gate_proj=quant(h, i),
+                up_proj=quant(h, i), down_proj=quant(i, h),
+                attn_norm=torch.ones(h, dtype=torch.float32, device=device),
+                mlp_norm=torch.ones(h, dtype=torch.float32, device=device),
+                q_bias=None, k_bias=None, v_bias=None, q_norm=None, k_norm=None)
+            torch.cuda.empty_cache()
+
     rnd = lambda *shape: (torch.randn(shape, generator=gen, device=device,
                                       dtype=torch.float32) * std).to(dtype)
     cos, sin = rope_tables_on_device(config.max_position, config.head_dim, config.rope_base,
                                      device)
-    return SimpleNamespace(config=config, blocks=blocks, embedding=rnd(config.vocab_size, h),
+    return SimpleNamespace(config=config, blocks=blocks(), embedding=rnd(config.vocab_size, h),
                            final_norm=torch.ones(h, dtype=torch.float32, device=device),
                            lm_head=rnd(h, config.vocab_size), cos=cos, sin=sin)
 
@@ -136,10 +142,23 @@ class QuantizedTransformer:
 
         self.embedding = take(source.embedding)
         self.attn, self.mlp = [], []
+        # "fp8-native": fp8 weights with per-N scales whose activations are
+        # quantized per token to e4m3 and contracted on the tensor cores
+        native = scheme == "fp8-native"
+        qscheme, qaxis = ("fp8", 1) if native else (scheme, axis)
         for block in source.blocks:
-            qb = quantized_block(block, scheme, axis)
-            self.attn.append(ShardedAttention(qb, self.shard, device=self.device))
-            self.mlp.append(ShardedMLP(qb, self.shard, device=self.device))
+            qb = quantized_block(block, qscheme, qaxis)
+            attn = ShardedAttention(qb, self.shard, device=self.device)
+            mlp = ShardedMLP(qb, self.shard, device=self.device)
+            if native:
+                from . import _lib
+
+                for w in (attn.qkv, attn.q_proj, attn.k_proj, attn.v_proj, attn.o_proj,
+                          mlp.gate_up, mlp.down):
+                    if w is not None:
+                        w.act_quant = _lib.IE_ACT_FP8_TOKEN
+            self.attn.append(attn)
+            self.mlp.append(mlp)
             torch.cuda.empty_cache()
         self.final_norm = take(source.final_norm, torch.float32)
         vocab = self.config.vocab_size

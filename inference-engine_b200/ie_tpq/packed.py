@@ -42,7 +42,8 @@ class PackedWeight:
     """A quantized ``[K, N]`` weight resident in device memory."""
 
     def __init__(self, *, fmt: int, axis: int, k: int, n: int, codes, scale, zero=None,
-                 int4_symmetric: bool = False, gate_up: bool = False, unrepresentable: int = 0):
+                 int4_symmetric: bool = False, gate_up: bool = False, unrepresentable: int = 0,
+                 act_quant: int = 0):
         self.fmt = fmt
         self.axis = axis
         self.k = int(k)
@@ -60,6 +61,9 @@ class PackedWeight:
         self.int4_symmetric = bool(int4_symmetric)
         self.gate_up = bool(gate_up)
         self.unrepresentable = int(unrepresentable)
+        # how activations meet this weight (ie_qlinear_args.act_quant): 0 as
+        # given, IE_ACT_FP8_TOKEN per-token e4m3 (the "fp8-native" scheme)
+        self.act_quant = int(act_quant)
         self._struct = None
 
     # ---- description -----------------------------------------------------
@@ -194,7 +198,7 @@ class PackedWeight:
             zero = self.zero[:, n0:n1].contiguous()
         return PackedWeight(fmt=self.fmt, axis=self.axis, k=self.k, n=n1 - n0,
                             codes=self.codes[n0:n1], scale=scale, zero=zero,
-                            int4_symmetric=self.int4_symmetric)
+                            int4_symmetric=self.int4_symmetric, act_quant=self.act_quant)
 
     def slice_k(self, k0: int, k1: int) -> "PackedWeight":
         """Input rows [k0, k1) of the reference weight (a row shard); copies."""
@@ -213,7 +217,8 @@ class PackedWeight:
             scale = self.scale[k0 // 128:k1 // 128].contiguous()
             zero = self.zero[k0 // 128:k1 // 128].contiguous()
         return PackedWeight(fmt=self.fmt, axis=self.axis, k=k1 - k0, n=self.n, codes=codes,
-                            scale=scale, zero=zero, int4_symmetric=self.int4_symmetric)
+                            scale=scale, zero=zero, int4_symmetric=self.int4_symmetric,
+                            act_quant=self.act_quant)
 
     @staticmethod
     def pair_gate_up(gate: "PackedWeight", up: "PackedWeight") -> "PackedWeight":
@@ -234,7 +239,7 @@ class PackedWeight:
             zero = torch.stack([gate.zero, up.zero], dim=2).reshape(g, 2 * gate.n).contiguous()
         return PackedWeight(fmt=gate.fmt, axis=gate.axis, k=gate.k, n=2 * gate.n, codes=codes,
                             scale=scale, zero=zero, int4_symmetric=gate.int4_symmetric,
-                            gate_up=True)
+                            gate_up=True, act_quant=gate.act_quant)
 
 
 def concat_rows(parts: list["PackedWeight"]) -> "PackedWeight":
@@ -254,16 +259,18 @@ def concat_rows(parts: list["PackedWeight"]) -> "PackedWeight":
     return PackedWeight(fmt=first.fmt, axis=first.axis, k=first.k, n=sum(p.n for p in parts),
                         codes=torch.cat([p.codes for p in parts]).contiguous(),
                         scale=torch.cat([p.scale for p in parts], dim=dim).contiguous(), zero=zero,
-                        int4_symmetric=first.int4_symmetric)
+                        int4_symmetric=first.int4_symmetric, act_quant=first.act_quant)
 
 
 def quantize_on_device(w, scheme: str, axis: int | None = 0) -> "PackedWeight":
     """Quantize a ``[K, N]`` f32 CUDA tensor straight into the packed layout.
 
     ``scheme``: "int8" (symmetric, reference axis), "int4" (symmetric), "fp8"
-    (e4m3) or "int4-g128".  The tables are the same as the host path's
-    (``ie_tpq.weights``) but never leave the device -- the load path for
-    model-sized weights.
+    (e4m3), "int4-g128", or "fp8-native": e4m3 with one scale per output
+    channel (N) whose callers quantize activations per token to e4m3 and
+    contract both on the tensor cores (``act_quant``; ``axis`` is ignored).
+    The tables are the same as the host path's (``ie_tpq.weights``) but never
+    leave the device -- the load path for model-sized weights.
     """
     torch = require_cuda()
     if w.dim() != 2 or w.dtype != torch.float32 or not w.is_cuda:
@@ -295,6 +302,9 @@ def quantize_on_device(w, scheme: str, axis: int | None = 0) -> "PackedWeight":
             raise ValueError(f"{int(bad.item())} group scale/zero values are not representable in f16")
         return PackedWeight(fmt=_lib.IE_FMT_INT4, axis=_lib.IE_AXIS_GROUP128, k=k, n=n,
                             codes=packed, scale=s16, zero=z16)
+    act_quant = 0
+    if scheme == "fp8-native":
+        scheme, axis, act_quant = "fp8", 1, _lib.IE_ACT_FP8_TOKEN
     kaxis = -1 if axis is None else axis
     nscale = k if kaxis == 0 else (n if kaxis == 1 else 1)
     scale = torch.empty(nscale, dtype=torch.float32, device=dev)
@@ -320,4 +330,4 @@ def quantize_on_device(w, scheme: str, axis: int | None = 0) -> "PackedWeight":
                                 stream), "pack_weight")
     axis_id = {0: _lib.IE_AXIS_K, 1: _lib.IE_AXIS_N, -1: _lib.IE_AXIS_TENSOR}[kaxis]
     return PackedWeight(fmt=fmt, axis=axis_id, k=k, n=n, codes=packed, scale=scale,
-                        int4_symmetric=sym, unrepresentable=int(bad.item()))
+                        int4_symmetric=sym, unrepresentable=int(bad.item()), act_quant=act_quant)

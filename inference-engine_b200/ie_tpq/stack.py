@@ -67,6 +67,8 @@ def layer_weight_bytes(shape: DecoderShape, scheme: str, world: int) -> dict[str
             out[name] = k * n / 2 + (k // 128) * n * 4
         elif scheme == "int4":
             out[name] = k * n / 2 + 4 * k
+        elif scheme == "fp8-native":   # per-N scales
+            out[name] = k * n + 4 * n
         else:
             out[name] = k * n + 4 * k
     return out

@@ -85,7 +85,7 @@ def _own(p: PackedWeight) -> PackedWeight:
     return PackedWeight(fmt=p.fmt, axis=p.axis, k=p.k, n=p.n, codes=p.codes.clone(),
                         scale=p.scale.clone(), zero=p.zero.clone() if p.zero is not None else None,
                         int4_symmetric=p.int4_symmetric, gate_up=p.gate_up,
-                        unrepresentable=p.unrepresentable)
+                        unrepresentable=p.unrepresentable, act_quant=p.act_quant)
 
 
 def _f32(v, device):

@@ -47,7 +47,7 @@ def test_traffic_field_comes_from_the_committed_capture(bench):
     from types import SimpleNamespace
 
     shape = SimpleNamespace(hidden=4096, intermediate=14336)
-    args = SimpleNamespace(scheme="int4-g128", batch=16)
+    args = SimpleNamespace(scheme="int4-g128", batch=16, model="llama3-8b")
     h, i = shape.hidden, shape.intermediate
     tp1 = (h * 2 * i / 2 + (h // 128) * 2 * i * 4) + 16 * h * 2 + 16 * i * 2
     traffic, src = bench.measured_traffic(args, tp1, shape)
@@ -56,5 +56,6 @@ def test_traffic_field_comes_from_the_committed_capture(bench):
     assert abs(traffic - tp1) / tp1 < 0.01
     half, _ = bench.measured_traffic(args, tp1 / 2, shape)
     assert half == pytest.approx(traffic / 2)
-    other, why = bench.measured_traffic(SimpleNamespace(scheme="int8", batch=16), tp1, shape)
+    other, why = bench.measured_traffic(SimpleNamespace(scheme="int8", batch=16, model="llama3-8b"),
+                                        tp1, shape)
     assert other is None and "no capture" in why
