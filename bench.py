@@ -949,7 +949,8 @@ def _lib_act_fp8() -> int:
 def run_sweep(args, rank: int, world: int, local: int) -> None:
     """The isolated row-parallel sweep: y = all_reduce(x_shard @ W_shard) for W [K, N] split by
     K over the ranks, fused (qlinear with comm=) against two unfused builds,
-    all timed with CUDA events and taken as the max over ranks:
+    all timed as CUDA-graph replays with CUDA events and taken as the max
+    over ranks:
       * ``us_unfused`` -- dequantize the shard to bf16 on every call, cuBLAS GEMM,
         NCCL all-reduce (a quantized model served without a fused kernel);
       * ``us_dense`` -- the dequantized bf16 shard kept resident (the reference's
@@ -986,10 +987,33 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    inner = 8   # calls per captured graph
+
     def timed(fn, budget_ms: float = 60.0) -> float:
+        """ms per call of ``fn``: a CUDA graph of ``inner`` consecutive calls
+        is replayed, so host launch costs do not enter small cases while
+        consecutive kernels still overlap as in a model's step graph
+        (programmatic launch); max over ranks.  Eager calls if capture fails."""
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
+        per = 1
+        try:
+            g = torch.cuda.CUDAGraph()
+            s_ = torch.cuda.Stream()
+            s_.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s_):
+                fn()
+            torch.cuda.current_stream().wait_stream(s_)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g):
+                for _ in range(inner):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+            fn, per = g.replay, inner
+        except RuntimeError:
+            torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1007,7 +1031,7 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
             fn()
         b.record()
         torch.cuda.synchronize()
-        return max_over_ranks(a.elapsed_time(b) / reps)
+        return max_over_ranks(a.elapsed_time(b) / (reps * per))
 
     gen = torch.Generator(device="cuda")
     for scheme in formats:
