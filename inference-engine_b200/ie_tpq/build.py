@@ -30,19 +30,6 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def cutlass_include() -> list[str]:
-    """CuTe/CUTLASS headers vendored in site-packages (header-only use)."""
-    import site
-
-    dirs = []
-    for sp in site.getsitepackages():
-        for sub in ("flashinfer/data/cutlass/include",):
-            p = Path(sp) / sub
-            if p.exists():
-                dirs.append(str(p))
-    return dirs
-
-
 def command(out: Path) -> list[str]:
     cmd = [nvcc(), *ARCH, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
            "-shared", "-I", str(REPO / "include"), "-o", str(out)]

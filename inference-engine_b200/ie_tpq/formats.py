@@ -117,4 +117,4 @@ def format_id(fmt) -> int:
 
 
 __all__ = ["IntegerFormat", "FloatFormat", "INT8", "INT4", "INT8_ASYM", "FP8_E4M3", "FP8_E5M2",
-           "round_to_float_format", "format_id", "np"]
+           "round_to_float_format", "format_id"]

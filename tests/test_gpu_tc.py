@@ -1,8 +1,8 @@
 """Parity of the tcgen05 tensor-core path (algo=2) against the oracle.
 
-The A operand is the weight dequantized to the activation type (bf16/f16) in
-shared memory, so each weight carries one extra rounding of at most half an
-ulp of that type (2^-9 relative for bf16) before f32 accumulation; outputs are
+The A operand is the weight dequantized to f16 in tensor memory (TMEM), so
+each weight carries one extra rounding of at most half an ulp of f16 (2^-11
+relative) before f32 accumulation; outputs are
 held to the north-star tolerance rtol 2e-2 / atol 2e-3 against the
 reference's f32 dequantize-then-matmul, and to the same bound against the
 f32 weight-streaming kernel.  Split-K partials are summed in split order, so
