@@ -100,6 +100,8 @@ def parse():
                     help="the isolated row-parallel GEMM + all-reduce sweep (one JSON line per "
                          "case) instead of the decode step")
     ap.add_argument("--sweep-m", default="1,8,64,512,4096,16384")
+    ap.add_argument("--allreduce", choices=["auto", "oneshot", "twoshot"], default="auto",
+                    help="protocol of the fused all-reduce at N > 1 (the sweep times both)")
     ap.add_argument("--sweep-formats", default="int8,int4-g128,fp8,fp8-native")
     args = ap.parse_args()
     if args.layers is None:
@@ -293,6 +295,7 @@ def workload_config(args, world: int) -> dict:
             "model": f"{args.model}-shaped (random init)", "scheme": args.scheme,
             "global_batch": args.batch, "seq_len": 1, "layers": args.layers,
             "parallelism": f"tp{world}",
+            "allreduce": args.allreduce if world > 1 else None,
             "l2": "weights per rank exceed the 126 MB L2; no flush between steps"}
 
 
@@ -738,7 +741,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     comm = None
     if world > 1:
         comm = Communicator(rank, world, max_bytes=max(max(args.batch, 256) * shape.hidden * 4,
-                                                       1 << 20), timeout_s=10.0)
+                                                       1 << 20), timeout_s=10.0,
+                            algo=ALLREDUCE_ALGOS[args.allreduce])
     layers = [synthetic_layer(shape, args.scheme, shard, seed=1000 + li)
               for li in range(args.layers)]
     stack = LinearStack(shape, layers, args.batch, torch.bfloat16, comm=comm, world=world,
@@ -919,6 +923,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 # isolated fused row-parallel GEMM + all-reduce sweep
 # ---------------------------------------------------------------------------
 SWEEP_KN = ((14336, 4096), (28672, 8192))
+ALLREDUCE_ALGOS = {"auto": 0, "oneshot": 1, "twoshot": 2}   # ie_tpq.comm.AR_*
 NVLINK_GBS = 770.0   # measured B200 peer copy bandwidth, GB/s per direction
 
 
@@ -965,9 +970,13 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
     if world > 1:
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
         nccl = dist.new_group(backend="nccl")
-    from ie_tpq.comm import Communicator
+    from ie_tpq.comm import AR_ONESHOT, AR_TWOSHOT, Communicator, resolve_algo
     from ie_tpq.linear import qlinear
     from ie_tpq.packed import quantize_on_device
+
+    def resolve_name(world_, m_, n_):
+        tiles = -(-n_ // 128) * -(-m_ // 256)
+        return "oneshot" if resolve_algo(world_, tiles, m_ * n_) == AR_ONESHOT else "twoshot"
 
     ms_list = [int(v) for v in args.sweep_m.split(",")]
     formats = args.sweep_formats.split(",")
@@ -1054,8 +1063,8 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
                 x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
                 out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
 
-                def fused():
-                    qlinear(x, w, out=out, comm=comm, act_quant=act)
+                def fused(algo=None):
+                    qlinear(x, w, out=out, comm=comm, act_quant=act, reduce_algo=algo)
 
                 def unfused():
                     wd = w.dequantize("nk", torch.bfloat16)
@@ -1069,6 +1078,19 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
                         dist.all_reduce(y, group=nccl)
 
                 us_fused = timed(fused) * 1e3
+                protocols = {}
+                if world > 1:
+                    # both protocols, and the NVLink bytes each sends per rank
+                    # (f32 partials; two-shot's finished tiles also f32)
+                    for name, code in (("oneshot", AR_ONESHOT), ("twoshot", AR_TWOSHOT)):
+                        us = timed(lambda: fused(code)) * 1e3
+                        tiles = -(-n // 128) * -(-m // 256)
+                        used = resolve_algo(world, tiles, m * n, code)
+                        sent = (m * n * 4 * (world - 1) if used == AR_ONESHOT
+                                else m * n * 8 * (world - 1) / world)
+                        protocols[name] = {"us": us, "ran": "oneshot" if used == AR_ONESHOT
+                                           else "twoshot", "nvlink_bytes_sent": sent,
+                                           "nvlink_gbs": sent / (us * 1e3)}
                 us_unfused = timed(unfused) * 1e3
                 us_dense = timed(dense) * 1e3
                 b = sweep_bounds(scheme, m, k, n, world, w.nbytes, peaks)
@@ -1084,7 +1106,9 @@ def run_sweep(args, rank: int, world: int, local: int) -> None:
                                      "peak_source": peak_src,
                                      "nvlink_gbs": NVLINK_GBS},
                         "hbm_bytes": b["hbm_bytes"], "flops": b["flops"],
-                        "nvlink_bytes": b["nvlink_bytes"]}), flush=True)
+                        "nvlink_bytes": b["nvlink_bytes"],
+                        "allreduce_auto": protocols and resolve_name(world, m, n),
+                        "protocols": protocols}), flush=True)
                 del x, out
             del w, w_dense
             torch.cuda.empty_cache()

@@ -28,8 +28,9 @@
 extern "C" {
 #endif
 
-#define IE_TPQ_ABI_VERSION 3   /* 2: ie_qlinear_args gained norm_weight / norm_eps;
-                                  3: its last field became act_quant */
+#define IE_TPQ_ABI_VERSION 4   /* 2: ie_qlinear_args gained norm_weight / norm_eps;
+                                  3: its last field became act_quant;
+                                  4: ie_qlinear_allreduce / ie_allreduce take an algo */
 
 /* ---- status codes --------------------------------------------------- */
 #define IE_OK 0
@@ -118,6 +119,30 @@ typedef struct ie_qlinear_args {
  * workspace (ie_qlinear_workspace_size) only; else IE_ERR_INVALID. */
 #define IE_ACT_NONE 0
 #define IE_ACT_FP8_TOKEN 1
+
+/* All-reduce protocols of ie_qlinear_allreduce / ie_allreduce (the `algo` argument).
+ * Both sum the ranks' f32 partials in rank order, so they give bitwise equal
+ * outputs, identical on every rank (ie/parallel/sharding.py:40-44).
+ *   IE_AR_ONESHOT: every rank pushes each output tile's partial to every rank over
+ *     NVLink and every rank sums all of them: one flag round trip, (world-1) * 4
+ *     bytes sent per output element per rank.  Lowest latency (decode).
+ *   IE_AR_TWOSHOT: tile t belongs to rank t % world; partials go to the owner only,
+ *     the owner sums them, applies bias and residual and pushes the finished
+ *     tile to the other ranks: two flag round trips, 8 * (world-1) / world bytes
+ *     per element per rank.  Needs at least `world` output tiles (one tile is 128
+ *     output columns by up to 256 tokens on the tensor-core path); with fewer it
+ *     runs one-shot.
+ *   IE_AR_AUTO: one-shot below world 4 (two-shot sends as many bytes at world 2)
+ *     and below ~2.5 MB of NVLink bytes saved per rank; two-shot above.
+ *   IE_AR_NVLS (NVLink SHARP multicast) is not built: IE_ERR_UNSUPPORTED. */
+#define IE_AR_AUTO 0
+#define IE_AR_ONESHOT 1
+#define IE_AR_TWOSHOT 2
+#define IE_AR_NVLS 3
+/* The protocol IE_AR_AUTO (or `algo`) resolves to for a call of `world` ranks
+ * over `tiles` output tiles and `numel` output elements: IE_AR_ONESHOT or
+ * IE_AR_TWOSHOT; -1 for an unknown or unsupported algo.  Host-only, no GPU. */
+int ie_allreduce_resolve(int32_t world, int64_t tiles, int64_t numel, int32_t algo);
 
 /* ---- library ------------------------------------------------------------ */
 int ie_version(void);
@@ -256,11 +281,12 @@ int ie_comm_check(ie_comm* c);
  * its own K-shard (ie/parallel/sharding.py:60-66) and gets the reduced
  * out = [residual +] sum_r x_r @ W_r [+ bias] (ie/parallel/tensor_parallel.py:70,73).
  * Partials cross NVLink as f32 with P2P stores from the GEMM epilogue and are
- * summed in rank order, so every rank's output is bitwise identical. */
-int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* stream);
-/* Standalone all-reduce of a device tensor (same one-shot P2P protocol). */
+ * summed in rank order, so every rank's output is bitwise identical.  algo:
+ * IE_AR_* (above); every rank must pass the same algo and shapes. */
+int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, int32_t algo, void* stream);
+/* Standalone all-reduce of a device tensor (same protocols; a tile is 2048 elements). */
 int ie_allreduce(ie_comm* c, const void* in, void* out, int64_t numel, int32_t dtype,
-                 void* stream);
+                 int32_t algo, void* stream);
 
 #ifdef __cplusplus
 }

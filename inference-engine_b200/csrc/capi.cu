@@ -126,7 +126,8 @@ extern "C" int ie_kernel_status(uint32_t* bits, int32_t clear) {
   return IE_OK;
 }
 
-extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* stream) {
+extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, int32_t algo,
+                                    void* stream) {
   IE_CHECK(c && a, "qlinear_allreduce: null pointer");
   int rc = validate_linear(*a);
   if (rc || a->m == 0) return rc;
@@ -135,7 +136,7 @@ extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* 
   IE_CHECK(!a->w.gate_up, "qlinear_allreduce: gate/up pairs are column-parallel");
   if (use_tc(*a)) {
     ReduceCtx ctx;
-    rc = comm_context(c, &ctx, tc_tiles(*a), a->m * a->w.n);
+    rc = comm_context(c, &ctx, tc_tiles(*a), a->m * a->w.n, algo);
     if (rc) return rc;
     return launch_qlinear_tc(*a, &ctx, as_stream(stream));
   }
@@ -147,7 +148,7 @@ extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, void* 
   if (rc) return rc;
   IE_CHECK(resident > 0, "qlinear_allreduce: kernel cannot be resident on this device");
   ReduceCtx ctx;
-  rc = comm_context(c, &ctx, gemv_tiles(*a), a->m * a->w.n);
+  rc = comm_context(c, &ctx, gemv_tiles(*a), a->m * a->w.n, algo);
   if (rc) return rc;
   return launch_qlinear_gemv(*a, &ctx, resident, as_stream(stream));
 }

@@ -35,8 +35,25 @@ namespace ie {
 
 constexpr int64_t kMaxTiles = 1 << 16;
 
-int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_rank) {
+// Smallest NVLink saving per rank (bytes) for which IE_AR_AUTO takes two-shot:
+// about the cost of its second flag round trip at the measured ~770 GB/s.
+constexpr double kTwoShotMinSavedBytes = 2.5e6;
+
+int resolve_algo(int32_t world, int64_t tiles, int64_t numel, int32_t algo) {
+  if (algo == IE_AR_ONESHOT) return kArOneShot;
+  if (algo == IE_AR_TWOSHOT) return tiles >= world ? kArTwoShot : kArOneShot;
+  if (algo != IE_AR_AUTO) return -1;
+  if (world < 4 || tiles < world) return kArOneShot;
+  const double saved = (double)numel * (4.0 * (world - 1) - 8.0 * (world - 1) / world);
+  return saved >= kTwoShotMinSavedBytes ? kArTwoShot : kArOneShot;
+}
+
+int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_rank,
+                 int32_t algo) {
   IE_CHECK(c && c->open, "comm: not open (call ie_comm_open first)");
+  if (algo == IE_AR_NVLS)
+    return set_error(IE_ERR_UNSUPPORTED, "comm: the NVLS (multicast) all-reduce is not built");
+  IE_CHECK(algo >= IE_AR_AUTO && algo <= IE_AR_TWOSHOT, "comm: unknown all-reduce algo %d", algo);
   IE_CHECK(tiles <= kMaxTiles, "comm: %lld tiles exceed the flag table (%lld)",
            (long long)tiles, (long long)kMaxTiles);
   IE_CHECK(floats_per_rank <= c->slot_floats,
@@ -61,6 +78,7 @@ int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_ra
   rc->slot_floats = c->slot_floats;
   rc->rank = c->rank;
   rc->world = c->world;
+  rc->algo = resolve_algo(c->world, tiles, floats_per_rank, algo);
   return IE_OK;
 }
 
@@ -76,40 +94,29 @@ allreduce_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t n, Reduc
   const int64_t tiles = (n + kARTile - 1) / kARTile;
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int64_t b = t * kARTile;
+    int d0, d1;
+    ar_push_range(rc, t, d0, d1);
     for (int i = threadIdx.x; i < kARTile; i += kARThreads) {
       const int64_t e = b + i;
       if (e >= n) break;
       const float v = to_f32<T>(in[e]);
-      for (int dst = 0; dst < rc.world; ++dst)
+      for (int dst = d0; dst < d1; ++dst)
         landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + e] = v;
     }
     __syncthreads();
-    // st.release.sys publishes the block's pushes: bar.sync orders them before
-    // this thread's release, and a peer's ld.acquire.sys of the flag then sees them
-    if (threadIdx.x < rc.world)
-      st_release_sys(rc.flags[threadIdx.x] + t * kMaxWorld + rc.rank, epoch);
+    ar_publish(rc, t, epoch, threadIdx.x);
   }
+  // the flat array as one token row of n values, tile t = [t * kARTile, ...)
   __shared__ int s_ok;
-  const float* mine = landing_slot(rc, rc.rank, epoch);
-  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    if (threadIdx.x == 0) s_ok = 1;
-    __syncthreads();
-    if (threadIdx.x < rc.world &&
-        !bounded_wait_geq(rc.flags[rc.rank] + t * kMaxWorld + threadIdx.x, epoch,
-                          rc.timeout_ns, rc.status))
-      s_ok = 0;
-    __syncthreads();
-    if (!s_ok) break;   // the status word records the timeout
-    const int64_t b = t * kARTile;
-    for (int i = threadIdx.x; i < kARTile; i += kARThreads) {
-      const int64_t e = b + i;
-      if (e >= n) break;
-      float v = mine[e];
-      for (int src = 1; src < rc.world; ++src) v += mine[src * rc.slot_floats + e];
-      out[e] = from_f32<T>(v);
-    }
-    __syncthreads();
-  }
+  const ArOut o{out, nullptr, nullptr, n, 0, 1, n, dtype_of<T>(), false, false};
+  ar_finish_all<kARThreads>(rc, epoch, o, tiles,
+                            [](int64_t t, int64_t& n0, int& rows, int64_t& m0, int& cols) {
+                              n0 = t * kARTile;
+                              rows = kARTile;
+                              m0 = 0;
+                              cols = 1;
+                            },
+                            &s_ok);
   __syncthreads();
   reduce_finish(rc, epoch);
 }
@@ -126,10 +133,11 @@ int resident_allreduce_ctas(int* out) {
 }
 
 template <typename T>
-int launch_allreduce(ie_comm* c, const void* in, void* out, int64_t n, cudaStream_t s) {
+int launch_allreduce(ie_comm* c, const void* in, void* out, int64_t n, int32_t algo,
+                     cudaStream_t s) {
   const int64_t tiles = (n + kARTile - 1) / kARTile;
   ReduceCtx rc;
-  int rcode = comm_context(c, &rc, tiles, n);
+  int rcode = comm_context(c, &rc, tiles, n, algo);
   if (rcode) return rcode;
   int resident = 0;
   rcode = resident_allreduce_ctas<T>(&resident);
@@ -247,15 +255,22 @@ extern "C" int ie_comm_check(ie_comm* c) {
   return IE_OK;
 }
 
+extern "C" int ie_allreduce_resolve(int32_t world, int64_t tiles, int64_t numel,
+                                    int32_t algo) {
+  if (world < 1 || world > kMaxWorld || tiles < 0 || numel < 0) return -1;
+  const int r = resolve_algo(world, tiles, numel, algo);
+  return r == kArTwoShot ? IE_AR_TWOSHOT : r == kArOneShot ? IE_AR_ONESHOT : -1;
+}
+
 extern "C" int ie_allreduce(ie_comm* c, const void* in, void* out, int64_t numel, int32_t dtype,
-                            void* stream) {
+                            int32_t algo, void* stream) {
   IE_CHECK(c, "allreduce: null comm");
   IE_CHECK(numel >= 0, "allreduce: negative size");
   if (numel == 0) return IE_OK;
   IE_CHECK(in && out, "allreduce: null pointer");
   cudaStream_t s = as_stream(stream);
-  if (dtype == IE_DT_F32) return launch_allreduce<float>(c, in, out, numel, s);
-  if (dtype == IE_DT_BF16) return launch_allreduce<__nv_bfloat16>(c, in, out, numel, s);
-  if (dtype == IE_DT_F16) return launch_allreduce<__half>(c, in, out, numel, s);
+  if (dtype == IE_DT_F32) return launch_allreduce<float>(c, in, out, numel, algo, s);
+  if (dtype == IE_DT_BF16) return launch_allreduce<__nv_bfloat16>(c, in, out, numel, algo, s);
+  if (dtype == IE_DT_F16) return launch_allreduce<__half>(c, in, out, numel, algo, s);
   return set_error(IE_ERR_INVALID, "allreduce: unsupported dtype %d", dtype);
 }

@@ -85,6 +85,11 @@ template <> __device__ __forceinline__ __half from_f32<__half>(float v) {
   return __float2half_rn(v);
 }
 
+template <typename T> __host__ __device__ constexpr int dtype_of();
+template <> __host__ __device__ constexpr int dtype_of<float>() { return IE_DT_F32; }
+template <> __host__ __device__ constexpr int dtype_of<__nv_bfloat16>() { return IE_DT_BF16; }
+template <> __host__ __device__ constexpr int dtype_of<__half>() { return IE_DT_F16; }
+
 // ---- memory-model helpers for peer flags ---------------------------------------
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -122,7 +127,7 @@ __device__ __forceinline__ bool bounded_wait_geq(const uint32_t* flag, uint32_t 
   }
 }
 
-// ---- one-shot all-reduce context passed by value into fused kernels -----------------
+// ---- fused all-reduce context passed by value into the kernels ---------------------
 // The epoch that pairs pushes with waits lives in device memory: every fused
 // kernel reads it at start (epoch = *epoch_dev + 1, landing parity = epoch & 1)
 // and the last CTA to finish stores it back.  Host code never tracks it, so a
@@ -139,6 +144,7 @@ struct ReduceCtx {
   int64_t slot_floats;         // floats per source-rank slot in a landing buffer
   int32_t rank;
   int32_t world;
+  int32_t algo;                // kArOneShot or kArTwoShot (resolved on the host)
 };
 
 __device__ __forceinline__ uint32_t reduce_epoch(const ReduceCtx& rc) {
@@ -160,6 +166,185 @@ __device__ __forceinline__ void reduce_finish(const ReduceCtx& rc, uint32_t epoc
   }
 }
 
+// ---- the two in-kernel protocols ------------------------------------------------
+// One-shot (IE_AR_ONESHOT): every rank pushes each tile's f32 partial into slot
+//   [rank] of every rank's landing buffer and raises flags[tile][rank] there;
+//   every rank waits for all slots of every tile and sums them in rank order.
+//   NVLink bytes sent per rank: (world - 1) * 4 per element.
+// Two-shot (IE_AR_TWOSHOT): tile t belongs to rank t % world.  A rank pushes a
+//   tile's partial to its owner only (reduce-scatter); the owner sums the slots
+//   in rank order, applies bias and residual, stores its own output and pushes
+//   the finished f32 values into slot [owner] of every other rank's landing
+//   buffer, raising flags[t][owner] there (all-gather); the others round them
+//   to the output type.  NVLink bytes sent per rank: 8 (world - 1) / world per
+//   element, one more flag round trip.  The sum order is the same, so both
+//   protocols give bitwise equal outputs.  Two-shot needs tiles >= world: then
+//   every rank receives something from every peer in every call, which is what
+//   keeps the double-buffered landing parity safe (a rank starts call e + 2
+//   only after each peer has finished call e).
+// A flag word (rank x, tile t, source s) carries the partial of s when x owns t
+// (or in one-shot), and the finished tile when s owns t and x does not; the
+// two uses never meet in one call.
+constexpr int kArOneShot = 1;
+constexpr int kArTwoShot = 2;
+
+// Landing buffers that receive tile t's partial: [d0, d1).
+__device__ __forceinline__ void ar_push_range(const ReduceCtx& rc, int64_t t, int& d0, int& d1) {
+  if (rc.algo == kArTwoShot) {
+    d0 = (int)(t % rc.world);
+    d1 = d0 + 1;
+  } else {
+    d0 = 0;
+    d1 = rc.world;
+  }
+}
+// Raises tile t's partial flags; call after a CTA barrier that follows every
+// push of the tile (st.release.sys then publishes them: the barrier orders the
+// block's stores before this thread's release, and a peer's ld.acquire.sys of
+// the flag sees them).
+__device__ __forceinline__ void ar_publish(const ReduceCtx& rc, int64_t t, uint32_t epoch,
+                                           int tid) {
+  int d0, d1;
+  ar_push_range(rc, t, d0, d1);
+  if (tid < d1 - d0) st_release_sys(rc.flags[d0 + tid] + t * kMaxWorld + rc.rank, epoch);
+}
+
+__device__ __forceinline__ float ar_load(const void* p, int dt, int64_t i) {
+  if (dt == IE_DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == IE_DT_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return static_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void ar_store(void* p, int dt, int64_t i, float v) {
+  if (dt == IE_DT_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dt == IE_DT_F16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else static_cast<float*>(p)[i] = v;
+}
+
+// Where the reduced tiles go: out[m * ldo + n] = [residual[m * ldr + n] +]
+// (sum + [bias[n]]) for tokens m < M and rows n < N; landing offsets are m * N + n.
+struct ArOut {
+  void* out;
+  const void* residual;
+  const float* bias;
+  int64_t ldo, ldr, M, N;
+  int dtype;
+  bool has_bias, has_res;
+};
+
+// Finishes tile t = rows [n0, n0 + rows) x tokens [m0, m0 + cols) of a fused
+// all-reduce with all kT threads of the CTA: one-shot and the two-shot owner
+// wait for every rank's partial and sum them in rank order (the owner then
+// pushes the finished values to the other ranks); a two-shot non-owner waits
+// for the owner's values.  kPer elements per thread are loaded together, so a
+// round costs one memory round trip, not one per element.  Returns false when
+// a wait expired (the status word records it); every thread gets the same answer.
+template <int kT>
+__device__ bool ar_finish_tile(const ReduceCtx& rc, uint32_t epoch, const ArOut& o, int64_t t,
+                               int64_t n0, int rows, int64_t m0, int cols, int* s_ok) {
+  const int tid = threadIdx.x;
+  const bool two = rc.algo == kArTwoShot;
+  const int owner = two ? (int)(t % rc.world) : rc.rank;
+  const bool owns = owner == rc.rank;
+  if (tid == 0) *s_ok = 1;
+  __syncthreads();
+  if (owns) {
+    if (tid < rc.world &&
+        !bounded_wait_geq(rc.flags[rc.rank] + t * kMaxWorld + tid, epoch, rc.timeout_ns,
+                          rc.status))
+      *s_ok = 0;
+  } else if (tid == 0 &&
+             !bounded_wait_geq(rc.flags[rc.rank] + t * kMaxWorld + owner, epoch, rc.timeout_ns,
+                               rc.status)) {
+    *s_ok = 0;
+  }
+  __syncthreads();
+  if (!*s_ok) return false;
+  const float* mine = landing_slot(rc, rc.rank, epoch);
+  const float* src0 = mine + (owns ? 0 : (int64_t)owner * rc.slot_floats);
+  constexpr int kPer = 8;
+  const int count = rows * cols;
+  // element e of the tile: row n0 + e % rows, token m0 + e / rows; only e is
+  // kept per element and the rest recomputed, which keeps this tail of the
+  // fused kernels within their register budget
+  auto at = [&](int e, int64_t ld) { return (m0 + e / rows) * ld + (n0 + e % rows); };
+  auto ok = [&](int e) { return e < count && m0 + e / rows < o.M && n0 + e % rows < o.N; };
+  for (int e0 = tid; e0 < count; e0 += kT * kPer) {
+    float v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = e0 + j * kT;
+      v[j] = ok(e) ? __ldcg(src0 + at(e, o.N)) : 0.0f;
+    }
+    if (owns) {
+      float r[kPer];
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int e = e0 + j * kT;
+        r[j] = (o.has_res && ok(e)) ? ar_load(o.residual, o.dtype, at(e, o.ldr)) : 0.0f;
+      }
+      for (int src = 1; src < rc.world; ++src) {
+        const float* slot = mine + (int64_t)src * rc.slot_floats;
+        float w[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int e = e0 + j * kT;
+          w[j] = ok(e) ? __ldcg(slot + at(e, o.N)) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) v[j] += w[j];
+      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int e = e0 + j * kT;
+        if (o.has_bias) v[j] += ok(e) ? o.bias[n0 + e % rows] : 0.0f;
+        if (o.has_res) v[j] = r[j] + v[j];
+      }
+      if (two) {
+        for (int dst = 0; dst < rc.world; ++dst) {
+          if (dst == rc.rank) continue;
+          float* peer = landing_slot(rc, dst, epoch) + (int64_t)rc.rank * rc.slot_floats;
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) {
+            const int e = e0 + j * kT;
+            if (ok(e)) peer[at(e, o.N)] = v[j];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = e0 + j * kT;
+      if (ok(e)) ar_store(o.out, o.dtype, at(e, o.ldo), v[j]);
+    }
+  }
+  __syncthreads();
+  if (two && owns && tid < rc.world && tid != rc.rank)
+    st_release_sys(rc.flags[tid] + t * kMaxWorld + rc.rank, epoch);
+  return true;
+}
+
+// Phase 2 of a fused all-reduce over `tiles` tiles for the whole grid: a
+// two-shot rank finishes the tiles it owns first (they unblock the peers),
+// then copies out the rest.  tile(t, n0, rows, m0, cols) describes tile t.
+template <int kT, typename TileFn>
+__device__ void ar_finish_all(const ReduceCtx& rc, uint32_t epoch, const ArOut& o, int64_t tiles,
+                              TileFn tile, int* s_ok) {
+  const bool two = rc.algo == kArTwoShot;
+  for (int pass = 0; pass < (two ? 2 : 1); ++pass) {
+    // pass 0 of two-shot: owned tiles rank, rank + world, ...; otherwise all
+    // tiles (pass 1 skips the owned ones)
+    const int64_t count = (two && pass == 0) ? (tiles - rc.rank + rc.world - 1) / rc.world : tiles;
+    for (int64_t i = blockIdx.x; i < count; i += gridDim.x) {
+      const int64_t t = (two && pass == 0) ? rc.rank + i * rc.world : i;
+      if (two && pass == 1 && t % rc.world == rc.rank) continue;
+      int64_t n0, m0;
+      int rows, cols;
+      tile(t, n0, rows, m0, cols);
+      if (!ar_finish_tile<kT>(rc, epoch, o, t, n0, rows, m0, cols, s_ok)) return;
+    }
+  }
+}
+
 // ---- internal launchers (defined in the .cu files) ---------------------------------
 int validate_qweight(const ie_qweight& w);
 int launch_qlinear_gemv(const ie_qlinear_args& a, const ReduceCtx* rc, int max_ctas,
@@ -175,7 +360,9 @@ uint32_t tc_read_status(bool clear);
 // The tensor-core call with its split-K scratch in the library's static device
 // array instead of a caller workspace (ie_qlinear_noalloc); allocates nothing.
 int launch_qlinear_tc_static(const ie_qlinear_args& a, cudaStream_t s);
-// Fills rc for a collective call of comm c after checking its limits.
-int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_rank);
+// Fills rc for a collective call of comm c after checking its limits, with
+// the protocol for `algo` (IE_AR_*) resolved for this call's tile count and size.
+int comm_context(ie_comm* c, ReduceCtx* rc, int64_t tiles, int64_t floats_per_rank,
+                 int32_t algo);
 
 }  // namespace ie

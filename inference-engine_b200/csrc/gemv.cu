@@ -320,8 +320,10 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
     }
     __syncthreads();
     const int64_t nbase = rb * kTileRows;
-    for (int i = threadIdx.x; i < rc.world * MT * kTileRows; i += kThreads) {
-      const int dst = i / (MT * kTileRows);
+    int d0, d1;
+    ar_push_range(rc, t, d0, d1);
+    for (int i = threadIdx.x; i < (d1 - d0) * MT * kTileRows; i += kThreads) {
+      const int dst = d0 + i / (MT * kTileRows);
       const int e = i % (MT * kTileRows);
       const int m = e / kTileRows, rr = e % kTileRows;
       const int64_t gm = m0 + m, n = nbase + rr;
@@ -329,42 +331,23 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
         landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + gm * p.N + n] = tile[e];
     }
     __syncthreads();
-    // st.release.sys publishes the block's pushes: bar.sync orders them before
-    // this thread's release, and a peer's ld.acquire.sys of the flag then sees them
-    if (threadIdx.x < rc.world)
-      st_release_sys(rc.flags[threadIdx.x] + t * kMaxWorld + rc.rank, epoch);
+    ar_publish(rc, t, epoch, threadIdx.x);
   }
 
   if (!reduce) return;
 
-  // ---- phase 2: wait for every rank's partial of each tile, sum in rank order --
+  // ---- phase 2 (one-shot: every tile; two-shot: see ar_finish_all) --------------
   __shared__ int s_ok;
-  const float* mine = landing_slot(rc, rc.rank, epoch);
-  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int64_t rb = t % row_blocks, mc = t / row_blocks;
-    const int64_t m0 = mc * MT, nbase = rb * kTileRows;
-    if (threadIdx.x == 0) s_ok = 1;
-    __syncthreads();
-    if (threadIdx.x < rc.world) {
-      if (!bounded_wait_geq(rc.flags[rc.rank] + t * kMaxWorld + threadIdx.x, epoch,
-                            rc.timeout_ns, rc.status))
-        s_ok = 0;
-    }
-    __syncthreads();
-    if (!s_ok) break;   // status word already records the timeout
-    for (int e = threadIdx.x; e < MT * kTileRows; e += kThreads) {
-      const int m = e / kTileRows, rr = e % kTileRows;
-      const int64_t gm = m0 + m, n = nbase + rr;
-      if (gm >= p.M || n >= p.N) continue;
-      const int64_t off = gm * p.N + n;
-      float v = mine[off];
-      for (int src = 1; src < rc.world; ++src) v += mine[src * rc.slot_floats + off];
-      if (p.epilogue & IE_EPI_BIAS) v += p.bias[n];
-      if (p.epilogue & IE_EPI_RESIDUAL) v = load_act(p.residual, p.out_dtype, gm * p.ldr + n) + v;
-      store_out(p.out, p.out_dtype, gm * p.ldo + n, v);
-    }
-    __syncthreads();
-  }
+  const ArOut o{p.out, p.residual, p.bias, p.ldo, p.ldr, p.M, p.N, p.out_dtype,
+                (p.epilogue & IE_EPI_BIAS) != 0, (p.epilogue & IE_EPI_RESIDUAL) != 0};
+  ar_finish_all<kThreads>(rc, epoch, o, tiles,
+                          [=](int64_t t, int64_t& n0, int& rows, int64_t& m0, int& cols) {
+                            n0 = (t % row_blocks) * kTileRows;
+                            rows = kTileRows;
+                            m0 = (t / row_blocks) * MT;
+                            cols = MT;
+                          },
+                          &s_ok);
   __syncthreads();
   reduce_finish(rc, epoch);
 }

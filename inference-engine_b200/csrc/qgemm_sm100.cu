@@ -873,6 +873,7 @@ struct Epi {
   const ReduceCtx& rc;
   uint32_t epoch;
   int reduce;
+  int d0, d1;   // landing buffers that receive this tile's partial (reduce)
   // Writes the finished values of the 8 tokens m0 .. m0+7 of row n; gate/up
   // pairs combine lanes (n even, n+1).  Every shuffle, then every residual
   // load, is issued before the stores, so the loads of one token do not wait
@@ -921,7 +922,7 @@ struct Epi {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           if (m0 + j < p.M)
-            for (int dst = 0; dst < rc.world; ++dst)
+            for (int dst = d0; dst < d1; ++dst)
               landing_slot(rc, dst, epoch)[rc.rank * rc.slot_floats + (m0 + j) * p.N + n] = v[j];
       } else {
         const float b = (p.epilogue & IE_EPI_BIAS) ? p.bias[n] : 0.0f;
@@ -1462,7 +1463,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         if (p.axis == IE_AXIS_N) nscale = p.scale[n];
         else if (p.axis == IE_AXIS_TENSOR) nscale = p.scale[p.gate_up ? (n & 1) : 0];
       }
-      const Epi epi{p, rc, epoch, reduce};
+      const int tile_id = mt * p.n_tiles + nt;
+      int d0 = 0, d1 = 0;
+      if (reduce) ar_push_range(rc, tile_id, d0, d1);
+      const Epi epi{p, rc, epoch, reduce, d0, d1};
       // accumulators holding this unit: issuers that took at least one sub-stage
       const int nacc = p.chains * min(p.issuers, ks1 - ks0);
       constexpr bool csplit = CSPLIT;
@@ -1542,7 +1546,6 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       }
       if (dt == 0) mbar_arrive(accempty);
 
-      const int tile_id = mt * p.n_tiles + nt;
       bool finalize_here = !split;
       if constexpr (csplit) {
         finalize_here = crank == 0;
@@ -1628,11 +1631,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           ok = false;
           break;
         }
-        // st.release.sys publishes every dequant thread's pushes: the mbarrier
-        // above (release/acquire at CTA scope) orders them before this release,
-        // and a peer's ld.acquire.sys of the flag then sees them
-        if (dt < rc.world)
-          st_release_sys(rc.flags[dt] + (int64_t)tile_id * kMaxWorld + rc.rank, epoch);
+        // the barrier above orders every dequant thread's pushes before the
+        // releases
+        ar_publish(rc, tile_id, epoch, dt);
       }
     }
     if (!ok) *abort_flag = 1;
@@ -1657,65 +1658,19 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   }
 
   if (reduce) {
-    // ---- all-reduce phase 2: wait for every rank's tile, sum in rank order ----
+    // ---- all-reduce phase 2 (one-shot: every tile; two-shot: see ar_finish_all)
     __shared__ int s_ok;
-    const float* mine = landing_slot(rc, rc.rank, epoch);
-    const int tiles = p.n_tiles * p.m_tiles;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      if (threadIdx.x == 0) s_ok = 1;
-      __syncthreads();
-      if (threadIdx.x < rc.world &&
-          !bounded_wait_geq(rc.flags[rc.rank] + (int64_t)t * kMaxWorld + threadIdx.x, epoch,
-                            rc.timeout_ns, rc.status))
-        s_ok = 0;
-      __syncthreads();
-      if (!s_ok) break;
-      const int nt = t % p.n_tiles, mt = t / p.n_tiles;
-      // kPer elements per thread and round, all of whose loads (every rank's
-      // slot, the residual) are in flight together: one L2 round trip per round
-      // instead of one per element; ranks still add in rank order
-      constexpr int kPer = 8;
-      for (int e0 = threadIdx.x; e0 < kTileN * p.bn; e0 += kThreads * kPer) {
-        int64_t off[kPer], n[kPer], m[kPer];
-        bool valid[kPer];
-        float v[kPer];
-  #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int e = e0 + j * kThreads;
-          n[j] = (int64_t)nt * kTileN + (e % kTileN);
-          m[j] = (int64_t)mt * p.bn + (e / kTileN);
-          valid[j] = e < kTileN * p.bn && m[j] < p.M && n[j] < p.N;
-          off[j] = valid[j] ? m[j] * p.N + n[j] : 0;
-          v[j] = valid[j] ? __ldcg(mine + off[j]) : 0.0f;
-        }
-        const bool has_res = (p.epilogue & IE_EPI_RESIDUAL) != 0;
-        float r[kPer];
-  #pragma unroll
-        for (int j = 0; j < kPer; ++j)
-          r[j] = (has_res && valid[j]) ? load_val(p.residual, p.out_dtype, m[j] * p.ldr + n[j])
-                                       : 0.0f;
-        for (int src = 1; src < rc.world; ++src) {
-          const float* slot = mine + (int64_t)src * rc.slot_floats;
-          float w[kPer];
-  #pragma unroll
-          for (int j = 0; j < kPer; ++j) w[j] = valid[j] ? __ldcg(slot + off[j]) : 0.0f;
-  #pragma unroll
-          for (int j = 0; j < kPer; ++j) v[j] += w[j];
-        }
-        if (p.epilogue & IE_EPI_BIAS) {
-  #pragma unroll
-          for (int j = 0; j < kPer; ++j) v[j] += valid[j] ? p.bias[n[j]] : 0.0f;
-        }
-        if (has_res) {
-  #pragma unroll
-          for (int j = 0; j < kPer; ++j) v[j] = r[j] + v[j];
-        }
-  #pragma unroll
-        for (int j = 0; j < kPer; ++j)
-          if (valid[j]) store_val(p.out, p.out_dtype, m[j] * p.ldo + n[j], v[j]);
-      }
-      __syncthreads();
-    }
+    const ArOut o{p.out, p.residual, p.bias, p.ldo, p.ldr, p.M, p.N, p.out_dtype,
+                  (p.epilogue & IE_EPI_BIAS) != 0, (p.epilogue & IE_EPI_RESIDUAL) != 0};
+    const int n_tiles = p.n_tiles, bn = p.bn;
+    ar_finish_all<kThreads>(rc, epoch, o, (int64_t)p.n_tiles * p.m_tiles,
+                            [=](int64_t t, int64_t& n0, int& rows, int64_t& m0, int& cols) {
+                              n0 = (t % n_tiles) * kTileN;
+                              rows = kTileN;
+                              m0 = (t / n_tiles) * bn;
+                              cols = bn;
+                            },
+                            &s_ok);
     __syncthreads();
     reduce_finish(rc, epoch);
   }

@@ -40,6 +40,8 @@ IE_EPI_RESIDUAL = 2
 IE_EPI_SILU_MUL = 4
 IE_EPI_RMS_NORM = 8
 IE_ACT_NONE, IE_ACT_FP8_TOKEN = 0, 1
+# all-reduce protocols (the algo argument of ie_qlinear_allreduce / ie_allreduce)
+IE_AR_AUTO, IE_AR_ONESHOT, IE_AR_TWOSHOT, IE_AR_NVLS = 0, 1, 2, 3
 
 IE_COMM_HANDLE_BYTES = 64
 IE_QLINEAR_NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -52,7 +54,7 @@ EXPORTED = (
     "ie_rms_norm", "ie_rope_kv",
     "ie_reduce_partials", "ie_comm_create",
     "ie_comm_export", "ie_comm_open", "ie_comm_destroy", "ie_comm_set_timeout",
-    "ie_comm_check", "ie_qlinear_allreduce", "ie_allreduce",
+    "ie_comm_check", "ie_qlinear_allreduce", "ie_allreduce", "ie_allreduce_resolve",
 )
 
 
@@ -127,8 +129,9 @@ def _declare(lib: ctypes.CDLL) -> None:
         "ie_comm_destroy": (ctypes.c_int, [_P]),
         "ie_comm_set_timeout": (ctypes.c_int, [_P, ctypes.c_uint64]),
         "ie_comm_check": (ctypes.c_int, [_P]),
-        "ie_qlinear_allreduce": (ctypes.c_int, [_P, ctypes.POINTER(QLinearArgs), _P]),
-        "ie_allreduce": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _P]),
+        "ie_qlinear_allreduce": (ctypes.c_int, [_P, ctypes.POINTER(QLinearArgs), _I32, _P]),
+        "ie_allreduce": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P]),
+        "ie_allreduce_resolve": (ctypes.c_int, [_I32, _I64, _I64, _I32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -9,7 +9,10 @@ exchanged through ``torch.distributed`` (any backend, host objects only) and
 pushes its partial tiles straight into the peers' memory over NVLink.
 
 Every rank must issue the same collectives in the same order (the epoch that
-pairs pushes with waits advances once per call).
+pairs pushes with waits advances once per call), with the same protocol:
+``algo`` is one of ``AR_AUTO`` / ``AR_ONESHOT`` / ``AR_TWOSHOT`` (``ie_tpq.h``
+describes both protocols; they give bitwise equal results).  A communicator's
+``algo`` attribute is the default of every collective run through it.
 """
 from __future__ import annotations
 
@@ -17,6 +20,18 @@ import ctypes
 
 from . import _lib
 from .device import dtype_code, require_cuda
+
+AR_AUTO, AR_ONESHOT, AR_TWOSHOT, AR_NVLS = (_lib.IE_AR_AUTO, _lib.IE_AR_ONESHOT,
+                                            _lib.IE_AR_TWOSHOT, _lib.IE_AR_NVLS)
+
+
+def resolve_algo(world_size: int, tiles: int, numel: int, algo: int = AR_AUTO) -> int:
+    """The protocol ``algo`` resolves to for a collective of ``world_size``
+    ranks over ``tiles`` output tiles and ``numel`` elements (host only)."""
+    r = _lib.lib().ie_allreduce_resolve(world_size, tiles, numel, algo)
+    if r < 0:
+        raise ValueError(f"unknown or unsupported all-reduce algo {algo} (world {world_size})")
+    return r
 
 
 def gather_in_rank_order(own: bytes, world_size: int, group=None) -> bytes:
@@ -34,8 +49,10 @@ def gather_in_rank_order(own: bytes, world_size: int, group=None) -> bytes:
 
 class Communicator:
     def __init__(self, rank: int, world_size: int, device=None, max_bytes: int = 64 << 20,
-                 group=None, timeout_s: float = 2.0, _loopback: bool = False):
+                 group=None, timeout_s: float = 2.0, algo: int = AR_AUTO,
+                 _loopback: bool = False):
         torch = require_cuda()
+        self.algo = int(algo)
         if world_size < 1:
             raise ValueError("world_size must be at least 1")
         if not 0 <= rank < world_size:
@@ -85,13 +102,15 @@ class Communicator:
         """Raise ie_tpq._lib.TimeoutError_ if a bounded peer wait ran out."""
         _lib.check(_lib.lib().ie_comm_check(self.handle), "comm")
 
-    def all_reduce(self, tensor, out=None, stream=None):
+    def all_reduce(self, tensor, out=None, stream=None, algo: int | None = None):
         """Sum of every rank's ``tensor`` (rank order, f32 arithmetic)."""
         torch = require_cuda()
         t = tensor.contiguous()
         out = torch.empty_like(t) if out is None else out
         _lib.check(_lib.lib().ie_allreduce(self.handle, t.data_ptr(), out.data_ptr(), t.numel(),
-                                           dtype_code(t.dtype), _lib.stream_ptr(stream)),
+                                           dtype_code(t.dtype),
+                                           self.algo if algo is None else int(algo),
+                                           _lib.stream_ptr(stream)),
                    "allreduce")
         return out
 

@@ -106,8 +106,9 @@ def build_args(x, w: PackedWeight, out, *, bias=None, residual=None, silu_mul=Fa
 def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | None = None,
             out=None, out_dtype=None, comm=None, algo: int = ALGO_AUTO, stream=None,
             workspace=None, norm_weight=None, norm_eps: float = 1e-6,
-            act_quant: int | None = None):
-    """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce.
+            act_quant: int | None = None, reduce_algo: int | None = None):
+    """``y = x @ deq(W)`` on the GPU; ``comm`` fuses the row-parallel all-reduce
+    (protocol ``reduce_algo``, default ``comm.algo``).
 
     x: CUDA tensor ``[M, K]`` (bf16 / f16 / f32).  bias: f32 ``[N]``.  residual:
     ``[M, N]`` of the output dtype, added after the reduction.  A gate/up pair
@@ -145,6 +146,7 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
     if comm is None:
         _lib.check(_lib.lib().ie_qlinear(ctypes.byref(a), s), "qlinear")
     else:
-        _lib.check(_lib.lib().ie_qlinear_allreduce(comm.handle, ctypes.byref(a), s),
+        algo = comm.algo if reduce_algo is None else int(reduce_algo)
+        _lib.check(_lib.lib().ie_qlinear_allreduce(comm.handle, ctypes.byref(a), algo, s),
                    "qlinear_allreduce")
     return out

@@ -21,7 +21,11 @@ pytestmark = pytest.mark.gpu
 CASES = (("int4-g128", 1024, 512, 4, "f32"), ("int8", 512, 256, 3, "f32"),
          ("fp8", 512, 384, 1, "f32"), ("int8", 256, 128, 17, "f32"),
          ("int4-g128", 8192, 1024, 16, "bf16"), ("int8", 4096, 512, 8, "bf16"),
-         ("fp8", 4096, 768, 32, "bf16"))
+         ("fp8", 4096, 768, 32, "bf16"), ("int4-g128", 4096, 4096, 64, "bf16"),
+         ("int8", 2048, 2048, 300, "bf16"))
+# each case runs with both all-reduce protocols: they sum in the same order,
+# so the two-shot outputs must equal the one-shot ones bit for bit (cases with
+# fewer output tiles than ranks run two-shot as one-shot)
 
 
 def _key(scheme, k, n, m, dt):
@@ -35,7 +39,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
 
     from ie_tpq import formats as F
     from ie_tpq import weights as W
-    from ie_tpq.comm import Communicator
+    from ie_tpq.comm import AR_TWOSHOT, Communicator
     from ie_tpq.linear import qlinear
     from ie_tpq.sharding import Shard, split_input_dim
     from oracle import tpq_oracle as o
@@ -65,11 +69,22 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
             y = qlinear(xs, shard, residual=r_t, comm=comm)
         comm.check()
         results[_key(scheme, k, n, m, dt)] = y.float().cpu().numpy()
+        for _ in range(3):
+            y2 = qlinear(xs, shard, residual=r_t, comm=comm, reduce_algo=AR_TWOSHOT)
+        comm.check()
+        results["ts_" + _key(scheme, k, n, m, dt)] = y2.float().cpu().numpy()
         # standalone all-reduce of the same partial
         part = qlinear(xs, shard)
         red = comm.all_reduce(part)
+        red2 = comm.all_reduce(part, algo=AR_TWOSHOT)
         comm.check()
         results["ar_" + _key(scheme, k, n, m, dt)] = red.float().cpu().numpy()
+        results["arts_" + _key(scheme, k, n, m, dt)] = red2.float().cpu().numpy()
+    # a standalone all-reduce large enough for two-shot at any world size
+    big = torch.from_numpy(o.seeded_activations(512, 1024, seed=rank)).cuda()
+    results["big_one"] = comm.all_reduce(big).cpu().numpy()
+    results["big_two"] = comm.all_reduce(big, algo=AR_TWOSHOT).cpu().numpy()
+    comm.check()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **results)
     dist.barrier()
     comm.close()
@@ -105,6 +120,13 @@ def test_fused_row_parallel_allreduce_across_gpus():
     for key in outs[0]:
         for r in range(1, world):
             assert np.array_equal(outs[0][key], outs[r][key]), key
+    for key in outs[0]:
+        if key.startswith("ts_") or key.startswith("arts_"):
+            one = key[3:] if key.startswith("ts_") else "ar_" + key[5:]
+            assert np.array_equal(outs[0][key], outs[0][one]), key
+    np.testing.assert_array_equal(outs[0]["big_one"], outs[0]["big_two"])
+    parts = [o.seeded_activations(512, 1024, seed=r) for r in range(world)]
+    np.testing.assert_array_equal(outs[0]["big_one"], o.all_reduce(parts))
     for scheme, k, n, m, dt in CASES:
         w = o.seeded_weight(k, n, seed=k + n)
         x = o.seeded_activations(m, k, seed=m)

@@ -128,8 +128,48 @@ def test_fused_allreduce_at_world_one_equals_the_plain_layer():
         comm.close()
 
 
-def test_peer_that_never_arrives_ends_in_a_timeout_status():
-    comm = Communicator.loopback(world_size=2, timeout_s=0.05)
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
+def test_fused_allreduce_protocols_at_world_one(algo):
+    """At world 1 the two-shot owner path (every tile owned, nothing pushed to
+    peers) must give the plain layer's result bit for bit, on both kernels."""
+    from ie_tpq.comm import AR_ONESHOT, AR_TWOSHOT
+
+    a = AR_TWOSHOT if algo == "twoshot" else AR_ONESHOT
+    comm = Communicator(0, 1, algo=a)
+    try:
+        for dt, k, n, m in ((torch.float32, 512, 256, 6), (torch.bfloat16, 1024, 512, 40)):
+            q = W.quantize_grouped(o.seeded_weight(k, n, seed=73))
+            p = q.packed()
+            x = torch.from_numpy(o.seeded_activations(m, k, seed=74)).cuda().to(dt)
+            res = torch.from_numpy(o.seeded_activations(m, n, seed=75)).cuda().to(dt)
+            bias = torch.from_numpy(o.seeded_activations(1, n, seed=76)[0]).cuda()
+            plain = qlinear(x, p, residual=res, bias=bias)
+            for _ in range(3):
+                assert torch.equal(plain, qlinear(x, p, residual=res, bias=bias, comm=comm))
+            big = torch.from_numpy(o.seeded_activations(64, 1000, seed=77)).cuda().to(dt)
+            assert torch.equal(comm.all_reduce(big), big)
+        comm.check()
+    finally:
+        comm.close()
+
+
+def test_nvls_protocol_is_reported_unsupported():
+    from ie_tpq.comm import AR_NVLS
+
+    comm = Communicator(0, 1)
+    try:
+        with pytest.raises(RuntimeError, match="NVLS"):
+            comm.all_reduce(torch.ones(4096, device="cuda"), algo=AR_NVLS)
+    finally:
+        comm.close()
+
+
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
+def test_peer_that_never_arrives_ends_in_a_timeout_status(algo):
+    from ie_tpq.comm import AR_ONESHOT, AR_TWOSHOT
+
+    comm = Communicator.loopback(world_size=2, timeout_s=0.05,
+                                 algo=AR_TWOSHOT if algo == "twoshot" else AR_ONESHOT)
     try:
         q = W.quantize_integer(o.seeded_weight(256, 64, seed=80), F.INT8)
         p = q.packed()
@@ -141,7 +181,7 @@ def test_peer_that_never_arrives_ends_in_a_timeout_status():
         # the context is still healthy: a normal layer runs and is correct
         y = qlinear(x, p).cpu().numpy()
         np.testing.assert_allclose(y, x.cpu().numpy() @ q.dequantized(), rtol=1e-4, atol=1e-5)
-        comm.all_reduce(torch.ones(10, device="cuda"))
+        comm.all_reduce(torch.ones(10000, device="cuda"))
         with pytest.raises(_lib.TimeoutError_):
             comm.check()
     finally:

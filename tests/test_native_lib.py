@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.ie_version() == 3
+    assert lib.ie_version() == 4
 
 
 def test_invalid_arguments_are_rejected_before_any_cuda_call():
@@ -49,6 +49,33 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call():
     assert lib.ie_comm_create(0, 9, 0, 1024, ctypes.byref(h)) == _lib.IE_ERR_INVALID
     assert lib.ie_comm_create(2, 2, 0, 1024, ctypes.byref(h)) == _lib.IE_ERR_INVALID
     assert lib.ie_reduce_partials(None, 1, None, 4, 2, None) == _lib.IE_ERR_INVALID
+
+
+def test_allreduce_protocol_resolution():
+    """IE_AR_AUTO keeps one-shot for decode-sized outputs and below world 4 (two-shot
+    sends as many bytes at world 2); two-shot needs one output tile per rank."""
+    from ie_tpq.comm import AR_AUTO, AR_NVLS, AR_ONESHOT, AR_TWOSHOT, resolve_algo
+
+    # decode: 16 tokens x 4096 columns, 32 tiles
+    for world in (1, 2, 4, 8):
+        assert resolve_algo(world, 32, 16 * 4096) == AR_ONESHOT
+    # prefill: 2048 tokens x 4096 columns
+    assert resolve_algo(2, 256, 2048 * 4096) == AR_ONESHOT
+    assert resolve_algo(4, 256, 2048 * 4096) == AR_TWOSHOT
+    assert resolve_algo(8, 256, 2048 * 4096) == AR_TWOSHOT
+    # the crossover at world 8: 2.5 MB saved = 21 bytes per element
+    assert resolve_algo(8, 64, 119_000) == AR_ONESHOT
+    assert resolve_algo(8, 64, 120_000) == AR_TWOSHOT
+    # explicit choices; two-shot with fewer tiles than ranks runs one-shot
+    assert resolve_algo(2, 32, 64, AR_TWOSHOT) == AR_TWOSHOT
+    assert resolve_algo(8, 4, 1 << 24, AR_TWOSHOT) == AR_ONESHOT
+    assert resolve_algo(8, 4096, 1 << 24, AR_ONESHOT) == AR_ONESHOT
+    with pytest.raises(ValueError):
+        resolve_algo(8, 64, 1 << 20, AR_NVLS)
+    with pytest.raises(ValueError):
+        resolve_algo(9, 64, 1 << 20, AR_AUTO)
+    lib = _lib.lib()
+    assert lib.ie_allreduce(None, None, None, 4, 2, 0, None) == _lib.IE_ERR_INVALID
 
 
 def test_status_codes_map_to_the_reference_exceptions():
