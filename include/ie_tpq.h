@@ -192,12 +192,13 @@ int ie_dequantize(const ie_qweight* w, int32_t layout, int32_t out_dtype, void* 
  * (ie/model/torch_transformer.py:36-38,60) and torch_backend.swiglu
  * (ie/kernels/torch_backend.py:125-127) on a packed shard. */
 /* Bytes of caller-owned workspace the call would use with the tensor-core
- * kernel: 256 bytes of grid-barrier words (offset 0), the split-K tile
- * tickets, the activations converted once per launch (bf16 -> f16, RMS norm
- * folded in) and the split-K partials.  The workspace must be zero-filled
- * before its first use; afterwards the barrier words stay consistent by
- * themselves (also after a launch that gave up on an expired wait), and the
- * call clears the tickets on the stream before a split-K kernel runs.  A
+ * kernel: 256 bytes of grid-barrier and launch-generation words (offset 0),
+ * the split-K tile tickets, the activations converted once per launch (bf16 ->
+ * f16, RMS norm folded in) and the split-K partials.  The workspace must be
+ * zero-filled before its first use; afterwards those words stay consistent by
+ * themselves (also after a launch that gave up on an expired wait), and every
+ * ticket carries the tag of the launch that counted it, so leftovers of an
+ * earlier launch are ignored and nothing is cleared between calls.  A
  * smaller workspace (or none) runs the best plan that fits: split-K without
  * the activation pre-pass, the pre-pass without split-K, or neither. */
 size_t ie_qlinear_workspace_size(const ie_qlinear_args* a);

@@ -32,10 +32,12 @@
 //               run the epilogue: split-K reduction in split order, per-N /
 //               per-tensor scale, bias, SiLU*up, residual, store or all-reduce.
 //
-// Work units are (row tile, token tile, K split); CTAs loop over them.  A
-// split writes its f32 partial to the caller's workspace and the last split to
-// arrive (atomic ticket) sums all splits in split order, so results do not
-// depend on scheduling.  Every mbarrier wait is bounded (SM clock cycles); on
+// Work units are (row tile, token tile, K split); CTAs loop over them, or, in
+// the stream-K order, each CTA takes an equal contiguous range of the
+// (tile, K stage) order and a tile shared by several ranges is split between
+// them.  A split writes its f32 partial to the caller's workspace and the last
+// split to arrive (tagged atomic ticket) sums all splits in split order, so
+// results do not depend on scheduling.  Every mbarrier wait is bounded (SM clock cycles); on
 // expiry the kernel records an error bit, drains its TMA copies and MMAs, frees
 // TMEM and returns.
 #include <cuda.h>
@@ -45,6 +47,7 @@
 #include <mutex>
 
 #include "common.cuh"
+
 
 namespace ie {
 namespace tc {
@@ -68,6 +71,7 @@ constexpr int kACols = kBK / 2; // TMEM columns of one A stage (two f16 per colu
 constexpr int kMaxAStages = 6;
 constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 2 GHz
 constexpr int kMinSmem = 120 * 1024;              // keeps one CTA per SM
+constexpr size_t kTicketBytes = 128 * 1024;       // workspace ticket region: 32768 tiles
 
 // F_FP8N: fp8 weights contracted natively with per-token fp8 activations
 // (IE_ACT_FP8_TOKEN): no dequantization, A read by the MMA from shared memory.
@@ -106,7 +110,9 @@ struct TcParams {
   int nclusters;            // clusters in the grid (csplit)
   int recv_bytes;           // csplit: leader's receive buffer [splits-1][bn][128] f32
   float* ws;                // split-K partials [splits][M][N]
-  uint32_t* counters;       // per (m_tile, n_tile) tickets, self-resetting
+  uint32_t* counters;       // per (m_tile, n_tile) tickets, tagged with the launch (below)
+  int streamk;              // stream-K order: CTA b takes TMA stages [b T / G, (b+1) T / G)
+                            // of the tile-major (tile, stage) order, T = tiles * stages
   // RMS-norm prologue: x rows (plain loads for the per-token sum of squares)
   // and the f32 weight over K; the x tiles are scaled while they are converted
   const void* x;
@@ -122,6 +128,11 @@ struct TcParams {
   // advances; waiters wait for it to leave the value read at kernel start.
   // Every CTA arrives exactly once (at teardown if it gave up before), so
   // the words are consistent for the next launch without being cleared.
+  // xbar[2] is the launch generation of the split-K tickets and xbar[3] counts
+  // the CTAs that finished: the last one advances xbar[2] and clears xbar[3].
+  // A ticket word holds (tag << 8) | arrivals, tag = generation % (2^24 - 1) + 1:
+  // a word left by another launch (one that gave up part-way included) carries
+  // another tag and counts as zero, so tickets need no clearing between launches.
   __half* xh;               // F_FP8N: the e4m3 codes of x, [M][K] bytes
   uint32_t* xbar;
   float* xs;                // F_FP8N: per-token activation scales [M]
@@ -278,6 +289,24 @@ __device__ __forceinline__ uint32_t ticket_add(uint32_t* p) {
   uint32_t old;
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
   return old;
+}
+// Tagged ticket (see TcParams::xbar): the arrivals of launch `tag` before this
+// one.  An arrival that finds another launch's tag installs (tag << 8) with
+// one compare-and-swap against the value it read, which fails harmlessly when
+// another arrival got there first (a word never returns to a stale value
+// within a launch); the count itself is an atomic add, acquire-release at GPU
+// scope like ticket_add, so arrivals never retry.
+__device__ __forceinline__ uint32_t ticket_tagged(uint32_t* p, uint32_t tag) {
+  const uint32_t cur = *reinterpret_cast<volatile uint32_t*>(p);
+  if ((cur >> 8) != tag) {
+    uint32_t prev;
+    asm volatile("atom.cas.relaxed.gpu.global.b32 %0, [%1], %2, %3;"
+                 : "=r"(prev)
+                 : "l"(p), "r"(cur), "r"(tag << 8)
+                 : "memory");
+    (void)prev;
+  }
+  return ticket_add(p) & 0xFFu;
 }
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
@@ -986,9 +1015,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfree + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(abort_flag) + 1;
-  float* s_rinv = reinterpret_cast<float*>(s_ticket + 1);   // [bn] RMS-norm prologue
+  // [max(bn, kDqWarps)]: RMS factors of a token tile, or of one pre-pass round
+  float* s_rinv = reinterpret_cast<float*>(s_ticket + 1);
   // pre-pass barrier: [0] generation at kernel start, [1] this CTA has arrived
-  volatile uint32_t* s_xb = reinterpret_cast<volatile uint32_t*>(s_rinv + p.bn);
+  volatile uint32_t* s_xb =
+      reinterpret_cast<volatile uint32_t*>(s_rinv + (p.bn > kDqWarps ? p.bn : kDqWarps));
   auto xbar_arrive = [&]() {
     if (ticket_add(p.xbar) == gridDim.x - 1u) {
       *reinterpret_cast<volatile uint32_t*>(p.xbar) = 0u;   // ordered by the release below
@@ -1001,7 +1032,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   pdl_launch_dependents();
   // The all-reduce epoch, the pre-pass barrier generation and the pre-pass's
   // reads of x all depend on the previous kernel: such launches wait at once.
-  // The others overlap their prologue and first weight stages with it.
+  // The others overlap their prologue and first weight stages with it; their
+  // split-K partials, tickets and ticket generation are touched only in an
+  // epilogue, after MMAs that read x tiles the producer loads only after its
+  // own wait, and by thread 0 (the producer) after that wait.
   if (reduce || XPRE) pdl_wait();
   const uint32_t epoch = reduce ? reduce_epoch(rc) : 0u;
 
@@ -1054,14 +1088,43 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   // split-K, the cluster steps through tiles and CTA rank r takes split r.
   const int tiles_all = p.n_tiles * p.m_tiles;
   const int crank = CSPLIT ? (int)cluster_rank() : 0;
-  const int u_first = CSPLIT ? (int)(blockIdx.x / p.splits) + tiles_all * crank : (int)blockIdx.x;
-  const int u_step = CSPLIT ? p.nclusters : (int)gridDim.x;
-  const int u_end = CSPLIT ? tiles_all * (crank + 1) : units;
-  auto unit_range = [&](int u, int& nt, int& mt, int& ks0, int& ks1, int& sp) {
+  // Stream-K: CTA b takes the TMA stages [lo, hi) = [b T / G, (b+1) T / G) of
+  // the tile-major order (tile * tstages + stage, T = tiles * tstages), its
+  // units are the tiles that range touches, and the unit of tile t is segment
+  // (b - first CTA of t) of t's nsp segments.  (Never with cluster split-K.)
+  // (32-bit arithmetic: the plan keeps T * G below 2^31)
+  const bool sk = !CSPLIT && p.streamk;
+  const int sk_total = tiles_all * tstages;
+  const int sk_g = (int)gridDim.x, sk_b = (int)blockIdx.x;
+  const int sk_lo = sk ? sk_b * sk_total / sk_g : 0;
+  const int sk_hi = sk ? (sk_b + 1) * sk_total / sk_g : 0;
+  // the CTA whose range holds stage i
+  auto sk_cta = [&](int i) { return ((i + 1) * sk_g - 1) / sk_total; };
+  const int u_first = sk ? sk_lo / tstages
+                      : CSPLIT ? (int)(blockIdx.x / p.splits) + tiles_all * crank
+                               : (int)blockIdx.x;
+  const int u_step = sk ? 1 : CSPLIT ? p.nclusters : (int)gridDim.x;
+  const int u_end = sk ? (sk_hi - 1) / tstages + 1 : CSPLIT ? tiles_all * (crank + 1) : units;
+  // unit u: row tile nt, token tile mt, sub-stages [ks0, ks1), segment sp of nsp
+  auto unit_range = [&](int u, int& nt, int& mt, int& ks0, int& ks1, int& sp, int& nsp) {
+    if constexpr (!CSPLIT) {
+      if (sk) {
+        nt = u % p.n_tiles;
+        mt = u / p.n_tiles;
+        const int t0 = u * tstages;
+        ks0 = (max(sk_lo, t0) - t0) * sub;
+        ks1 = min(p.kstages, (min(sk_hi, t0 + tstages) - t0) * sub);
+        const int first = sk_cta(t0);
+        sp = sk_b - first;
+        nsp = sk_cta(t0 + tstages - 1) - first + 1;
+        return;
+      }
+    }
     nt = u % p.n_tiles;
     const int rest = u / p.n_tiles;
     mt = rest % p.m_tiles;
     sp = rest / p.m_tiles;
+    nsp = p.splits;
     const int per = (tstages + p.splits - 1) / p.splits;
     ks0 = sp * per * sub;
     ks1 = min(p.kstages, ks0 + per * sub);
@@ -1131,8 +1194,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         return true;
       };
       for (int u = u_first; u < u_end && ok && !*abort_flag; u += u_step) {
-        int nt, mt, ks0, ks1, sp;
-        unit_range(u, nt, mt, ks0, ks1, sp);
+        int nt, mt, ks0, ks1, sp, nsp;
+        unit_range(u, nt, mt, ks0, ks1, sp, nsp);
         for (int ks = ks0; ks < ks1; ks += sub, ++ti) {
           const int s = ti % ns;
           // reusing a slot needs the MMAs of stage ti - ns, hence its x tile
@@ -1213,8 +1276,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       int unit_i = 0;
       bool ok = true;
       for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
-        int nt, mt, ks0, ks1, sp;
-        unit_range(u, nt, mt, ks0, ks1, sp);
+        int nt, mt, ks0, ks1, sp, nsp;
+        unit_range(u, nt, mt, ks0, ks1, sp, nsp);
         if (!mbar_wait(accempty, (unit_i & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
@@ -1347,8 +1410,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     };
     int norm_mt = -1;   // token tile whose RMS factors s_rinv holds
     for (int u = u_first; u < u_end && ok; u += u_step, ++unit_i) {
-      int nt, mt, ks0, ks1, sp;
-      unit_range(u, nt, mt, ks0, ks1, sp);
+      int nt, mt, ks0, ks1, sp, nsp;
+      unit_range(u, nt, mt, ks0, ks1, sp, nsp);
       const int64_t n = (int64_t)nt * kTileN + row;
       if (p.norm_w && !XPRE && mt != norm_mt) {
         if (p.pdl) pdl_wait();   // the rows are the previous kernel's output
@@ -1457,7 +1520,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       }
       tc_fence_after();
       const int64_t m0 = (int64_t)mt * p.bn;
-      const bool split = p.splits > 1;
+      const bool split = nsp > 1;
       float nscale = 1.0f;
       if (n < p.N) {
         if (p.axis == IE_AXIS_N) nscale = p.scale[n];
@@ -1585,8 +1648,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           break;
         }
         if (dt == 0) {
-          const uint32_t t = ticket_add(&p.counters[tile_id]);
-          *s_ticket = (t == (uint32_t)(p.splits - 1)) ? 1 : 0;
+          // the generation changes only after every CTA of this launch is done
+          const uint32_t t = ticket_tagged(&p.counters[tile_id],
+                                           ld_acquire_gpu(p.xbar + 2) % 0xFFFFFFu + 1u);
+          *s_ticket = (t == (uint32_t)(nsp - 1)) ? 1 : 0;
         }
         if (!dq_sync()) {
           ok = false;
@@ -1600,7 +1665,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           for (int c0 = 8 * group; c0 < p.bn; c0 += 8 * kGroups) {
             float acc[8], res[8];
             epi.load_res8(m0 + c0, n, lane, res);
-            for (int q0 = 0; q0 < p.splits; q0 += 2) {
+            for (int q0 = 0; q0 < nsp; q0 += 2) {
               float v[2][8];
         #pragma unroll
               for (int qq = 0; qq < 2; ++qq) {
@@ -1608,22 +1673,21 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
                   const int64_t m = m0 + c0 + jj;
-                  v[qq][jj] = (q0 + qq < p.splits && m < p.M && n < p.N) ? __ldcg(part + m * p.N + n)
-                                                                          : 0.0f;
+                  v[qq][jj] = (q0 + qq < nsp && m < p.M && n < p.N) ? __ldcg(part + m * p.N + n)
+                                                                     : 0.0f;
                 }
               }
         #pragma unroll
               for (int qq = 0; qq < 2; ++qq)
         #pragma unroll
                 for (int jj = 0; jj < 8; ++jj)
-                  if (q0 + qq < p.splits) acc[jj] = (q0 + qq == 0) ? v[0][jj] : acc[jj] + v[qq][jj];
+                  if (q0 + qq < nsp) acc[jj] = (q0 + qq == 0) ? v[0][jj] : acc[jj] + v[qq][jj];
             }
         #pragma unroll
             for (int jj = 0; jj < 8; ++jj) acc[jj] *= nscale;
             token_scales(m0 + c0, acc);
             epi.emit8(m0 + c0, n, acc, lane, res);
           }
-          if (dt == 0) p.counters[tile_id] = 0u;
         }
       }
       if (reduce && finalize_here) {
@@ -1641,6 +1705,12 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
   // ------------------------------ teardown ------------------------------
   __syncthreads();
+  // the last CTA to finish advances the ticket generation for the next launch
+  // (every CTA's tickets precede its arrival here)
+  if (p.counters && threadIdx.x == 0 && ticket_add(p.xbar + 3) == gridDim.x - 1u) {
+    *reinterpret_cast<volatile uint32_t*>(p.xbar + 3) = 0u;   // ordered by the release below
+    st_release_gpu(p.xbar + 2, ld_acquire_gpu(p.xbar + 2) + 1u);
+  }
   // a CTA that gave up before arriving at the pre-pass barrier arrives now, so
   // the barrier words end every launch consistent (the error bit is set)
   if constexpr (XPRE) {
@@ -1711,6 +1781,8 @@ struct Plan {
   size_t xs_off = 0;         // F_FP8N: per-token activation scales [M] f32
   size_t part_off = 0;       // split-K partials [splits][M][N] f32
   bool csplit = false;       // splits of a tile as one thread-block cluster
+  bool streamk = false;      // stream-K order (splits = most CTAs sharing one tile)
+  int grid = 0;              // CTAs launched (clusters: the cluster count decides)
   bool xpre = false;         // activation pre-pass (bf16 or RMS-norm activations)
   int recv_bytes = 0;
 };
@@ -1779,7 +1851,7 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
     pl.sub /= 2;
   pl.w_stage_bytes = row_stage * kTileN * pl.sub;
   const int sms = sm_count();
-  constexpr double kUnitCost = 1.5, kFinalizeCost = 1.5;
+  constexpr double kUnitCost = 1.5, kFinalizeCost = 1.5, kSkUnitCost = 1.0;
   double best = 1e300;
   const int tiles = pl.n_tiles * pl.m_tiles;
   const int tst = (pl.kstages + pl.sub - 1) / pl.sub;   // TMA stages along K
@@ -1790,7 +1862,9 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
   const bool cluster_ok = pl.bn <= 8 * kGroups;
   constexpr double kClusterGain = 0.25;
   bool best_cluster = false;
-  for (int s = 1; s <= (allow_split ? 16 : 1); ++s) {
+  // (global split-K keeps one ticket per tile in the fixed ticket region)
+  const bool split_ok = allow_split && (size_t)tiles * 4 <= kTicketBytes;
+  for (int s = 1; s <= (split_ok ? 16 : 1); ++s) {
     if (s > 1 && tst < 2 * s) break;
     // every split must own at least one TMA stage: (s-1) * ceil(tst/s) < tst
     const int per = (tst + s - 1) / s;
@@ -1811,6 +1885,37 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
       best_cluster = true;
     }
   }
+  // Stream-K: one CTA per SM, each taking an equal contiguous range of the
+  // tile-major (tile, TMA stage) order, so no SM idles through a last partial
+  // wave; a tile shared by several ranges is finished by ticket from global
+  // partials.  The longest range pays a unit cost for every tile it touches.
+  // Measured on B200 it pays only for the native fp8 contraction over at
+  // least one full wave of tiles (Llama-3-70B gate/up at 32 tokens: 103 ->
+  // 93 us): where the dequant warps also run the epilogue (int4 / int8 / fp8
+  // dequantized), the extra segment epilogues and partials cost more than
+  // the tail they remove (Llama-3-8B int4 gate/up at 16 tokens: 37 -> 43 us),
+  // and on shorter grids the split plans already balance the SMs.
+  if (split_ok && native && tiles >= sms) {
+    const int64_t total = (int64_t)tiles * tst;
+    const int g = (int)std::min<int64_t>(sms, total);
+    // (the kernel's schedule arithmetic is 32-bit: (total + 1) * g < 2^31)
+    const bool fits32 = (total + 1) * g < (int64_t)1 << 31;
+    const int64_t q = total / g;   // stages of the shortest range
+    const double longest = std::ceil((double)total / g);
+    const int touched = (int)std::ceil(longest / tst) + 1;
+    const int max_seg = (int)((tst - 1 + q - 1) / q) + 1;
+    const double partial = 4.0 * (double)std::min<int64_t>(M, pl.bn) * kTileN * 4.0 /
+                           pl.w_stage_bytes;
+    const double t = longest + touched * kSkUnitCost + kFinalizeCost + partial;
+    if (fits32 && max_seg > 1 && t < best - 1e-9) {
+      best = t;
+      pl.streamk = true;
+      pl.splits = max_seg;
+      best_cluster = false;
+      pl.grid = g;
+    }
+  }
+  if (!pl.streamk) pl.grid = std::min(tiles * pl.splits, sms);
   int tbytes = 0;   // table bytes of a stage
   if (a.w.axis == IE_AXIS_GROUP128) {
     pl.t_kind = 1;
@@ -1857,17 +1962,20 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
   const size_t per = x_stage + pl.w_stage_bytes + pl.t_stage_bytes;
   pl.ns = (int)std::min<size_t>(12, (budget - fixed) / per);
   if (pl.ns < 2) pl.ns = 2;
-  // barriers, then TMEM slot, abort flag, ticket and the RMS factors [bn]
+  // barriers, then TMEM slot, abort flag, ticket, the RMS factors and the pre-pass words
   pl.smem = fixed + (size_t)pl.ns * per + 8 * (3 * pl.ns + 2 * pl.na + 2 + kMmaWarps + 3) + 16 +
-            4 * (size_t)pl.bn + 8;
+            4 * (size_t)std::max(pl.bn, kDqWarps) + 8;
   if (pl.smem < (size_t)kMinSmem) pl.smem = kMinSmem;   // one CTA per SM: TMEM and co-residency
-  // workspace: [pre-pass barrier words, 256 B | tile tickets | xh | split-K
-  // partials].  The barrier words sit at offset 0 for every plan and keep
-  // themselves consistent (zero on first use); the tickets are cleared by
-  // every launch that uses them.
-  const bool global_split = pl.splits > 1 && !pl.csplit;
+  // workspace: [barrier and generation words, 256 B | tile tickets | xh |
+  // split-K partials].  The words at offset 0 serve every plan and keep
+  // themselves consistent (zero on first use); the tickets carry the launch's
+  // tag, so they are never cleared.
+  const bool global_split = pl.splits > 1 && !pl.csplit;   // stream-K included
   pl.counters_off = 256;
-  pl.counters_bytes = global_split ? ((size_t)tiles * 4 + 255) / 256 * 256 : 0;
+  // a fixed ticket region for every plan that has a workspace: the words are
+  // only ever written as tickets (another plan's xh or partials never land
+  // there), so a leftover word always carries some launch's tag
+  pl.counters_bytes = kTicketBytes;
   pl.xh_off = pl.counters_off + pl.counters_bytes;
   const size_t xh_bytes = pl.xpre ? ((size_t)M * a.w.k * xe + 255) / 256 * 256 : 0;
   pl.xs_off = pl.xh_off + xh_bytes;
@@ -1916,7 +2024,6 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   }
   IE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)pl.smem));
-  const int units = pl.n_tiles * pl.m_tiles * pl.splits;
   ReduceCtx none{};
   const ReduceCtx ctx = rc ? *rc : none;
   const int reduce = rc ? 1 : 0;
@@ -1927,7 +2034,7 @@ int launch_typed(const ie_qlinear_args& a, const Plan& pl, const CUtensorMap& tw
   pdl_attr.val.programmaticStreamSerializationAllowed = 1;
   if (!pl.csplit) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min(units, sm_count()));
+    cfg.gridDim = dim3((unsigned)pl.grid);
     cfg.blockDim = dim3((unsigned)kThreads);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = s;
@@ -2126,15 +2233,13 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
   prm.sub = pl.sub;
   prm.csplit = pl.csplit ? 1 : 0;
   prm.recv_bytes = pl.recv_bytes;
+  prm.streamk = pl.streamk ? 1 : 0;
   if (pl.splits > 1 && !pl.csplit) {
+    // tickets tagged with the launch generation (TcParams::xbar): a launch that
+    // gave up part-way leaves counted tickets that the next launch ignores
     prm.counters = reinterpret_cast<uint32_t*>(ws + pl.counters_off);
     prm.ws = reinterpret_cast<float*>(ws + pl.part_off);
-    // The finalizing CTA of a tile resets its ticket, but a launch that gave up
-    // on an expired wait leaves the tickets of its unfinished tiles counted; a
-    // later launch on the same workspace would then finalize a tile before all
-    // of its splits arrived.  Clearing them first makes every launch start
-    // from zero whatever happened before.
-    IE_CUDA_TRY(cudaMemsetAsync(ws + pl.counters_off, 0, pl.counters_bytes, s));
+    prm.xbar = reinterpret_cast<uint32_t*>(ws);
   }
   prm.x_bf16 = a.act_dtype == IE_DT_BF16 ? 1 : 0;
   if (a.epilogue & IE_EPI_RMS_NORM) {
@@ -2146,9 +2251,8 @@ int launch_qlinear_tc(const ie_qlinear_args& a, const ReduceCtx* rc, cudaStream_
     prm.x = a.x;
     prm.ldx = a.ldx;
   }
-  // Every launch may overlap the previous kernel except one that clears its
-  // tickets first (the memset node sits between the two kernels).
-  prm.pdl = (pl.splits > 1 && !pl.csplit) ? 0 : 1;
+  // every launch may overlap the previous kernel's tail
+  prm.pdl = 1;
   if (pl.xpre) {
     prm.xh = reinterpret_cast<__half*>(ws + pl.xh_off);
     prm.xbar = reinterpret_cast<uint32_t*>(ws);
@@ -2220,9 +2324,9 @@ int launch_qlinear_tc_static(const ie_qlinear_args& a, cudaStream_t s) {
   b.workspace_bytes = IE_QLINEAR_NOALLOC_SCRATCH_BYTES;
   // launch_qlinear_tc runs the best plan whose scratch fits in the array
   // (fitting_plan: split-K and the activation pre-pass, the pre-pass alone, or
-  // neither) and clears the tile tickets first, so they read zero even after a
-  // call that ended early; the pre-pass barrier words (zero at module load)
-  // keep themselves consistent
+  // neither); its tile tickets carry the launch's tag and the barrier and
+  // generation words (zero at module load) keep themselves consistent, so a
+  // call that ended early leaves nothing to clear
   return launch_qlinear_tc(b, nullptr, s);
 }
 

@@ -16,10 +16,10 @@ from .packed import PackedWeight
 ALGO_AUTO, ALGO_GEMV, ALGO_TCGEN05 = 0, 1, 2
 
 # One workspace per device, grown on demand: split-K partials and tile
-# tickets, and the converted activations of the pre-pass.  Every launch clears
-# the ticket and barrier words it uses first, so consecutive calls on one
-# stream share it; calls on concurrent streams must pass their own
-# ``workspace=``.
+# tickets, and the converted activations of the pre-pass.  Zero-filled once;
+# its barrier and generation words stay consistent by themselves and the
+# tickets carry each launch's tag, so consecutive calls on one stream share it;
+# calls on concurrent streams must pass their own ``workspace=``.
 _WORKSPACE: dict = {}
 
 

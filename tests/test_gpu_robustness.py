@@ -1,8 +1,9 @@
 """Edge cases of the tensor-core kernel's state and number ranges.
 
 * A caller workspace whose ticket region holds leftovers (as a launch that gave
-  up on an expired wait would leave it) must not change the next result: the
-  call clears the tickets before a split-K launch.
+  up on an expired wait would leave it) must not change the next result: every
+  ticket word carries the tag of the launch that counted it, and a word with
+  another tag counts as zero.
 * bf16 activations beyond f16's range reach the tensor cores saturated to
   +-65504 (the activation operand is f16): outputs stay finite.
 * Small-magnitude weights (std 1e-3 and 1e-4, group scales near f16's
@@ -28,7 +29,7 @@ RTOL, ATOL = 2e-2, 2e-3
 
 @pytest.mark.parametrize("scheme,k,n,m", [("int4-g128", 4096, 1024, 64),
                                           ("int8-k", 4096, 6144, 16)])
-def test_stale_tickets_in_a_caller_workspace_are_cleared(scheme, k, n, m):
+def test_stale_tickets_in_a_caller_workspace_are_ignored(scheme, k, n, m):
     w = o.seeded_weight(k, n, seed=3)
     q, ref_w = quantize(scheme, w)
     p = q.packed()
@@ -39,15 +40,23 @@ def test_stale_tickets_in_a_caller_workspace_are_cleared(scheme, k, n, m):
     if need == 0:
         pytest.skip("this shape reduces its splits inside a cluster (no tickets)")
     ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
-    # every ticket counted once already: without the clear, the first split
-    # to arrive would finalize its tile from partial sums
-    ws[:256].view(torch.int32).fill_(1)
+    # the ticket words follow the 256 bytes of barrier and generation words;
+    # every ticket counted already: counted as such, the first split to arrive
+    # would finalize its tile from partial sums
+    tickets = ws[256:256 + 4 * 64].view(torch.int32)
+    tickets.fill_(1)
     y = qlinear(x, p, workspace=ws, algo=ALGO_TCGEN05).float().cpu().numpy()
     want = x.float().cpu().numpy() @ ref_w
     np.testing.assert_allclose(y, want, rtol=RTOL, atol=ATOL)
-    ws[:256].view(torch.int32).fill_(7)
+    tickets.fill_(7)
     y2 = qlinear(x, p, workspace=ws, algo=ALGO_TCGEN05).float().cpu().numpy()
     assert np.array_equal(y, y2)
+    # leftovers tagged by an earlier launch on this workspace (its tag is one
+    # below the current generation's): ignored too
+    gen = int(ws[8:12].view(torch.int32).item())
+    tickets.fill_(((gen - 1) % 0xFFFFFF + 1) << 8 | 1)
+    y3 = qlinear(x, p, workspace=ws, algo=ALGO_TCGEN05).float().cpu().numpy()
+    assert np.array_equal(y, y3)
 
 
 def test_bf16_activations_beyond_f16_range_saturate():
