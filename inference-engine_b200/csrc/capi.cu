@@ -52,7 +52,9 @@ int validate_linear(const ie_qlinear_args& a) {
   if (a.epilogue & IE_EPI_RMS_NORM) {
     IE_CHECK(a.norm_weight, "qlinear: RMS_NORM flag without a norm weight");
     IE_CHECK(a.norm_eps >= 0.0f, "qlinear: negative norm eps");
-    IE_CHECK(a.algo != 1, "qlinear: the fused RMS norm runs on the tensor-core path only");
+    IE_CHECK(a.algo != 1 || gemv_decode_ok(a),
+             "qlinear: the fused RMS norm runs on the tensor-core path, or on the "
+             "weight-streaming path for at most two tokens");
   }
   IE_CHECK(a.algo >= 0 && a.algo <= 2, "qlinear: unknown algo %d", a.algo);
   IE_CHECK(a.act_quant == IE_ACT_NONE || a.act_quant == IE_ACT_FP8_TOKEN,
@@ -71,16 +73,23 @@ int validate_linear(const ie_qlinear_args& a) {
   return IE_OK;
 }
 
-// Smallest token count routed to the tensor-core kernel under algo 0 (auto).
-// Measured on the Llama-3-8B shapes, the tcgen05 kernel is faster than the
-// weight-streaming one from a single token on (one decode layer: 98 us against
-// 119 us at TP=1), so every bf16/f16 batch takes it.
-constexpr int64_t kTcMinTokens = 1;
-
+// Auto routing (algo 0): every bf16/f16 batch takes the tensor-core kernel.
+// Measured on B200 over Llama-3-8B layers with distinct weights (nothing
+// reused from L2), the decode GEMV is slower from a single token on (o 14.6
+// against 13.3 us, gate/up 38.2 against 36.7 us); it serves algo 1 and f32
+// activations.
 bool use_tc(const ie_qlinear_args& a) {
   if (a.algo == 1) return false;
   if (a.algo == 2) return true;
-  return a.m >= kTcMinTokens && tc_usable(a);
+  return tc_usable(a);
+}
+
+// The fused all-reduce runs on the tensor-core kernel whenever it can (the
+// decode GEMV has no all-reduce; the general one streams far slower).
+bool use_tc_reduce(const ie_qlinear_args& a) {
+  if (a.algo == 1) return false;
+  if (a.algo == 2) return true;
+  return tc_usable(a);
 }
 
 }  // namespace
@@ -107,9 +116,10 @@ extern "C" int ie_qlinear(const ie_qlinear_args* a, void* stream) {
   int rc = validate_linear(*a);
   if (rc || a->m == 0) return rc;
   if (use_tc(*a)) return launch_qlinear_tc(*a, nullptr, as_stream(stream));
-  if (a->epilogue & IE_EPI_RMS_NORM)
+  if ((a->epilogue & IE_EPI_RMS_NORM) && !gemv_decode_ok(*a))
     return set_error(IE_ERR_UNSUPPORTED, "qlinear: the fused RMS norm needs bf16/f16 "
-                                         "activations, K %% 128 == 0 and aligned rows");
+                                         "activations, K %% 128 == 0 and aligned rows, or "
+                                         "at most two tokens");
   return launch_qlinear_gemv(*a, nullptr, 0, as_stream(stream));
 }
 
@@ -134,7 +144,7 @@ extern "C" int ie_qlinear_allreduce(ie_comm* c, const ie_qlinear_args* a, int32_
   IE_CHECK(!(a->epilogue & IE_EPI_SILU_MUL),
            "qlinear_allreduce: SILU_MUL belongs to the column-parallel gate/up layer");
   IE_CHECK(!a->w.gate_up, "qlinear_allreduce: gate/up pairs are column-parallel");
-  if (use_tc(*a)) {
+  if (use_tc_reduce(*a)) {
     ReduceCtx ctx;
     rc = comm_context(c, &ctx, tc_tiles(*a), a->m * a->w.n, algo);
     if (rc) return rc;

@@ -350,6 +350,9 @@ int validate_qweight(const ie_qweight& w);
 int launch_qlinear_gemv(const ie_qlinear_args& a, const ReduceCtx* rc, int max_ctas,
                         cudaStream_t s);
 int64_t gemv_tiles(const ie_qlinear_args& a);
+// the decode GEMV serves this call (at most two tokens, x' of the whole K in
+// shared memory; it also folds the RMS norm); without a fused all-reduce
+bool gemv_decode_ok(const ie_qlinear_args& a);
 int gemv_resident_ctas(const ie_qlinear_args& a, int* out);
 // tcgen05 tensor-core path (qgemm_sm100.cu)
 bool tc_usable(const ie_qlinear_args& a);

@@ -34,7 +34,11 @@ enum Variant { V_INT8 = 0, V_INT4SYM = 1, V_INT4G = 2, V_FP8 = 3 };
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kTileRows = kWarps * 2;
+constexpr int kRows = 4;                    // weight rows per warp
+constexpr int kTileRows = kWarps * kRows;
+
+// x' buffers the kernel may hold: two for gate/up pairs with per-K scales
+template <int V> __host__ __device__ constexpr int nbuf_max() { return 2; }
 
 template <int V> struct VecInfo {
   static constexpr int kElems = (V == V_INT4SYM || V == V_INT4G) ? 32 : 16;  // per 16 bytes
@@ -62,6 +66,10 @@ struct GemvParams {
   int64_t ldo;
   int out_dtype;
   int kc;                 // K elements staged per chunk
+  // decode kernel only: RMS norm folded into the staging of x'
+  // (x' = x * rinv_m * norm_w[k], rinv_m = 1 / sqrt(mean_k(x^2) + eps))
+  const float* norm_w;
+  float norm_eps;
 };
 
 __device__ __forceinline__ float load_act(const void* p, int dt, int64_t i) {
@@ -85,59 +93,54 @@ __device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
 
-// Accumulate one 16-byte vector of one row against MT token runs of x'.
-// `xr` points at the padded run for token 0; runs of successive tokens are
-// `xstride` floats apart.  Returns per-token dot products in part[].
+// Packed f32x2 FMA (sm_100): acc.{x,y} += a.{x,y} * b.{x,y}, each lane
+// rounded once like fmaf.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+
+// Word j (32 bits) of a row's 16-byte code vector against the matching K
+// values of x' (xw[m]: this word's K values of token m, as f32 pairs), added
+// into part[m] as f32 pairs.
+//   int4: the pair (8j+2p, 8j+2p+1) sits in nibbles (p, p+4); one mask+or
+//     makes a bf16x2 of 128 + q, whose halves are exact f32 (bits << 16);
+//   int8: byte i as f32 2^23 + 128 + q minus 2^23 + 128 (exact);
+//   fp8: e4m3 pairs widened through f16 (exact).
 template <int V, int MT>
-__device__ __forceinline__ void dot_vec(const uint4& wv, const float* __restrict__ xr,
-                                        int xstride, float (&part)[MT]) {
-  const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+__device__ __forceinline__ void dot_word(uint32_t w, const float2 (&xw)[MT][VecInfo<V>::kElems / 8],
+                                         float2 (&part)[MT]) {
   if constexpr (VecInfo<V>::kInt4) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int pp = 0; pp < 4; ++pp) {
+      const uint32_t t = ((w >> (4 * pp)) & 0x000F000Fu) | 0x43004300u;
+      const float2 q = make_float2(__uint_as_float(t << 16), __uint_as_float(t & 0xFFFF0000u));
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const uint32_t t = ((w4[j] >> (4 * p)) & 0x000F000Fu) | 0x43004300u;
-        const float lo = __uint_as_float(t << 16);           // 128 + q[k0 + 2p]
-        const float hi = __uint_as_float(t & 0xFFFF0000u);   // 128 + q[k0 + 2p + 1]
-        const int k = 8 * j + 2 * p;
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          const float2 xv = *reinterpret_cast<const float2*>(xr + m * xstride + k);
-          part[m] = fmaf(lo, xv.x, part[m]);
-          part[m] = fmaf(hi, xv.y, part[m]);
-        }
-      }
+      for (int m = 0; m < MT; ++m) part[m] = ffma2(q, xw[m][pp], part[m]);
     }
   } else if constexpr (V == V_INT8) {
+    const uint32_t u = w ^ 0x80808080u;   // q + 128 per byte
+    // 0x4B0000bb as f32 is 2^23 + b: subtracting 2^23 + 128 recovers q exactly
+    const float2 q0 = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - 8388736.0f,
+                                  __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - 8388736.0f);
+    const float2 q1 = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - 8388736.0f,
+                                  __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - 8388736.0f);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t u = w4[j] ^ 0x80808080u;   // q + 128 per byte
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        // 0x4B0000bb as f32 is 2^23 + b: subtracting 2^23 + 128 recovers q exactly
-        const float q = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440 | i)) - 8388736.0f;
-        const int k = 4 * j + i;
-#pragma unroll
-        for (int m = 0; m < MT; ++m) part[m] = fmaf(q, xr[m * xstride + k], part[m]);
-      }
+    for (int m = 0; m < MT; ++m) {
+      part[m] = ffma2(q0, xw[m][0], part[m]);
+      part[m] = ffma2(q1, xw[m][1], part[m]);
     }
   } else {  // V_FP8
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((w >> (16 * h)) & 0xFFFFu);
+      const float2 q = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3)));
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((w4[j] >> (16 * h)) & 0xFFFFu);
-        const __half2 hv = __half2(__nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3));
-        const float2 f = __half22float2(hv);
-        const int k = 4 * j + 2 * h;
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          const float2 xv = *reinterpret_cast<const float2*>(xr + m * xstride + k);
-          part[m] = fmaf(f.x, xv.x, part[m]);
-          part[m] = fmaf(f.y, xv.y, part[m]);
-        }
-      }
+      for (int m = 0; m < MT; ++m) part[m] = ffma2(q, xw[m][h], part[m]);
     }
   }
 }
@@ -164,11 +167,13 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int64_t rb = t % row_blocks, mc = t / row_blocks;
     const int64_t m0 = mc * MT;
-    const int64_t r0 = rb * kTileRows + warp * 2;          // this warp's two rows
-    const bool row_ok[2] = {r0 < p.N, r0 + 1 < p.N};
-    float acc[2][MT];
+    const int64_t r0 = rb * kTileRows + warp * kRows;      // this warp's rows
+    bool row_ok[kRows];
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
+    for (int r = 0; r < kRows; ++r) row_ok[r] = r0 + r < p.N;
+    float acc[kRows][MT];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
 #pragma unroll
       for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
 
@@ -204,14 +209,19 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
       }
 
       // ---- stream the weights of this chunk -------------------------------
+      // Every lane takes one 16-byte code vector of each of the warp's rows at
+      // a K position; the x' values of that position are read from shared
+      // memory once per word and token (16-byte loads) and serve all rows.
+      constexpr int kU = MT >= 4 ? 1 : 2;     // vectors per row in flight
+      constexpr int kXw = VI::kElems / 8;     // f32 pairs of x' per 32-bit word
       const int nvec = kce / VI::kElems;
-      for (int base = 0; base < nvec; base += 32 * 4) {
-        uint4 wv[4][2];
+      for (int base = 0; base < nvec; base += 32 * kU) {
+        uint4 wv[kU][kRows];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
           const int c = base + u * 32 + lane;
 #pragma unroll
-          for (int r = 0; r < 2; ++r) {
+          for (int r = 0; r < kRows; ++r) {
             if (c < nvec && row_ok[r])
               wv[u][r] = ldg_stream(p.codes + (r0 + r) * p.row_bytes +
                                     (k0 / VI::kElems + c) * 16);
@@ -220,33 +230,62 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
           const int c = base + u * 32 + lane;
           if (c >= nvec) continue;
+          float2 part[kRows][MT];
 #pragma unroll
-          for (int r = 0; r < 2; ++r) {
+          for (int r = 0; r < kRows; ++r)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) part[r][m] = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int b = 0; b < (nbuf_max<V>()); ++b) {
+              if (b >= nbuf) break;
+              // this word's K values of every token of buffer b
+              float2 xw[MT][kXw];
+#pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                const float4* xr = reinterpret_cast<const float4*>(
+                    xs + (b * MT + m) * xstride + c * VI::kPadded + j * (2 * kXw));
+#pragma unroll
+                for (int h = 0; h < kXw / 2; ++h) {
+                  const float4 v = xr[h];
+                  xw[m][2 * h] = make_float2(v.x, v.y);
+                  xw[m][2 * h + 1] = make_float2(v.z, v.w);
+                }
+              }
+#pragma unroll
+              for (int r = 0; r < kRows; ++r) {
+                if (nbuf == 2 && (r & 1) != b) continue;   // gate/up rows alternate buffers
+                const uint32_t w = j == 0 ? wv[u][r].x : j == 1 ? wv[u][r].y
+                                 : j == 2 ? wv[u][r].z : wv[u][r].w;
+                dot_word<V, MT>(w, xw, part[r]);
+              }
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) {
             if (!row_ok[r]) continue;
-            const int buf = (nbuf == 2) ? r : 0;
-            const float* xr = xs + buf * MT * xstride + c * VI::kPadded;
-            float part[MT];
-#pragma unroll
-            for (int m = 0; m < MT; ++m) part[m] = 0.0f;
-            dot_vec<V, MT>(wv[u][r], xr, xstride, part);
+            const int buf = (nbuf == 2) ? (r & 1) : 0;
             if constexpr (V == V_INT4G) {
               const int64_t g = (k0 + (int64_t)c * VI::kElems) / 128;
               const int64_t gi = g * p.N + (r0 + r);
-              const float s = __half2float(p.gscale[gi]);
+              const float sc = __half2float(p.gscale[gi]);
               const float off = 128.0f + __half2float(p.gzero[gi]);
 #pragma unroll
               for (int m = 0; m < MT; ++m)
-                acc[r][m] += s * (part[m] - off * xsum[(buf * MT + m) * runs + c]);
+                acc[r][m] += sc * ((part[r][m].x + part[r][m].y) -
+                                   off * xsum[(buf * MT + m) * runs + c]);
             } else if constexpr (V == V_INT4SYM) {
 #pragma unroll
               for (int m = 0; m < MT; ++m)
-                acc[r][m] += part[m] - 136.0f * xsum[(buf * MT + m) * runs + c];
+                acc[r][m] += (part[r][m].x + part[r][m].y) -
+                             136.0f * xsum[(buf * MT + m) * runs + c];
             } else {
 #pragma unroll
-              for (int m = 0; m < MT; ++m) acc[r][m] += part[m];
+              for (int m = 0; m < MT; ++m) acc[r][m] += part[r][m].x + part[r][m].y;
             }
           }
         }
@@ -256,7 +295,7 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
 
     // ---- lane reduction ---------------------------------------------------
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
+    for (int r = 0; r < kRows; ++r)
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         float v = acc[r][m];
@@ -267,11 +306,11 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
 
     // ---- scales that sit on N ------------------------------------------------
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < kRows; ++r) {
       if (!row_ok[r]) continue;
       float s = 1.0f;
       if (p.axis == IE_AXIS_N) s = p.scale[r0 + r];
-      else if (p.axis == IE_AXIS_TENSOR) s = p.scale[p.gate_up ? r : 0];
+      else if (p.axis == IE_AXIS_TENSOR) s = p.scale[p.gate_up ? (r & 1) : 0];
 #pragma unroll
       for (int m = 0; m < MT; ++m) acc[r][m] *= s;
     }
@@ -283,19 +322,23 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
           const int64_t gm = m0 + m;
           if (gm >= p.M) continue;
           if (p.epilogue & IE_EPI_SILU_MUL) {
-            if (!row_ok[1]) continue;
-            float g = acc[0][m], u = acc[1][m];
-            if (p.epilogue & IE_EPI_BIAS) {
-              g += p.bias[r0];
-              u += p.bias[r0 + 1];
+            // rows (r0 + 2i, r0 + 2i + 1) are a gate/up pair
+#pragma unroll
+            for (int i2 = 0; i2 < kRows / 2; ++i2) {
+              if (!row_ok[2 * i2 + 1]) continue;
+              float g = acc[2 * i2][m], u = acc[2 * i2 + 1][m];
+              if (p.epilogue & IE_EPI_BIAS) {
+                g += p.bias[r0 + 2 * i2];
+                u += p.bias[r0 + 2 * i2 + 1];
+              }
+              const int64_t j = r0 / 2 + i2;
+              float v = silu(g) * u;
+              if (p.epilogue & IE_EPI_RESIDUAL) v += load_act(p.residual, p.out_dtype, gm * p.ldr + j);
+              store_out(p.out, p.out_dtype, gm * p.ldo + j, v);
             }
-            const int64_t j = r0 / 2;
-            float v = silu(g) * u;
-            if (p.epilogue & IE_EPI_RESIDUAL) v += load_act(p.residual, p.out_dtype, gm * p.ldr + j);
-            store_out(p.out, p.out_dtype, gm * p.ldo + j, v);
           } else {
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
+            for (int r = 0; r < kRows; ++r) {
               if (!row_ok[r]) continue;
               const int64_t n = r0 + r;
               float v = acc[r][m];
@@ -313,10 +356,9 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
     // ---- fused all-reduce, phase 1: push this tile's partial to every rank --
     if (lane == 0) {
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        tile[m * kTileRows + warp * 2] = acc[0][m];
-        tile[m * kTileRows + warp * 2 + 1] = acc[1][m];
-      }
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) tile[m * kTileRows + warp * kRows + r] = acc[r][m];
     }
     __syncthreads();
     const int64_t nbase = rb * kTileRows;
@@ -350,6 +392,225 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
                           &s_ok);
   __syncthreads();
   reduce_finish(rc, epoch);
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMV (M <= 2 tokens, no fused all-reduce).  The general kernel above
+// stages x' chunk by chunk inside every 32-row tile (three CTA barriers per
+// chunk), so a warp has one round of weight loads in flight between
+// barriers.  Here x' for the whole K is staged once per CTA -- after the first
+// row group's weight loads are issued -- and every warp then walks row groups
+// of kRows rows (persistent grid) with no CTA barrier, each lane keeping
+// kDecVec 16-byte code vectors of each row in flight.
+// ---------------------------------------------------------------------------
+constexpr int kDecVec = 4;
+
+template <int V, int MT>
+__device__ __forceinline__ void dec_epilogue(const GemvParams& p, float (&acc)[kRows][MT],
+                                             int64_t r0) {
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    float s = 1.0f;
+    if (r0 + r < p.N) {
+      if (p.axis == IE_AXIS_N) s = p.scale[r0 + r];
+      else if (p.axis == IE_AXIS_TENSOR) s = p.scale[p.gate_up ? (r & 1) : 0];
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[r][m] *= s;
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    if (m >= p.M) continue;
+    if (p.epilogue & IE_EPI_SILU_MUL) {
+#pragma unroll
+      for (int i2 = 0; i2 < kRows / 2; ++i2) {
+        if (r0 + 2 * i2 + 1 >= p.N) continue;
+        float g = acc[2 * i2][m], u = acc[2 * i2 + 1][m];
+        if (p.epilogue & IE_EPI_BIAS) {
+          g += p.bias[r0 + 2 * i2];
+          u += p.bias[r0 + 2 * i2 + 1];
+        }
+        const int64_t j = r0 / 2 + i2;
+        float v = silu(g) * u;
+        if (p.epilogue & IE_EPI_RESIDUAL) v += load_act(p.residual, p.out_dtype, m * p.ldr + j);
+        store_out(p.out, p.out_dtype, m * p.ldo + j, v);
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        const int64_t n = r0 + r;
+        if (n >= p.N) continue;
+        float v = acc[r][m];
+        if (p.epilogue & IE_EPI_BIAS) v += p.bias[n];
+        if (p.epilogue & IE_EPI_RESIDUAL) v = load_act(p.residual, p.out_dtype, m * p.ldr + n) + v;
+        store_out(p.out, p.out_dtype, m * p.ldo + n, v);
+      }
+    }
+  }
+}
+
+template <int V, int MT>
+__global__ void __launch_bounds__(kThreads)
+gemv_dec_kernel(GemvParams p) {
+  using VI = VecInfo<V>;
+  constexpr int kXw = VI::kElems / 8;
+  extern __shared__ __align__(16) float smem[];
+  const int nvec = (int)(p.K / VI::kElems);            // 16-byte code vectors per row
+  const int xstride = nvec * VI::kPadded;              // floats per token per buffer
+  const int nbuf = (p.gate_up && p.axis == IE_AXIS_K) ? 2 : 1;
+  float* xs = smem;                                    // [nbuf][MT][xstride]
+  float* xsum = xs + nbuf * MT * xstride;              // [nbuf][MT][nvec] (int4 only)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t groups = (p.N + kRows - 1) / kRows;
+  const int64_t g_step = (int64_t)gridDim.x * kWarps;
+  int64_t g = (int64_t)blockIdx.x * kWarps + warp;
+
+  uint4 wv[kDecVec][kRows];
+  auto load_round = [&](int64_t grp, int c0) {
+    const int64_t r0 = grp * kRows;
+#pragma unroll
+    for (int u = 0; u < kDecVec; ++u) {
+      const int c = c0 + u * 32 + lane;
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        if (grp < groups && r0 + r < p.N && c < nvec)
+          wv[u][r] = ldg_stream(p.codes + (r0 + r) * p.row_bytes + (int64_t)c * 16);
+        else
+          wv[u][r] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  // the first round's weights do not depend on x: in flight while x' is staged
+  load_round(g, 0);
+  __shared__ float s_red[MT][kWarps];
+  __shared__ float s_rinv[MT];
+  if (p.norm_w) {
+    // per-token RMS factor, with the tensor-core prologue's operations
+    // (sum of squares in f32, then 1 / sqrt(ss / K + eps) correctly rounded)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      float ss = 0.0f;
+      if (m < p.M)
+        for (int kk = threadIdx.x; kk < (int)p.K; kk += kThreads) {
+          const float v = load_act(p.x, p.act_dtype, m * p.ldx + kk);
+          ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_red[m][warp] = ss;
+    }
+    __syncthreads();
+    if (threadIdx.x < MT) {
+      float ss = 0.0f;
+      for (int w = 0; w < kWarps; ++w) ss += s_red[threadIdx.x][w];
+      s_rinv[threadIdx.x] = 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.norm_eps));
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < MT * (int)p.K; i += kThreads) {
+    const int m = i / (int)p.K, kk = i % (int)p.K;
+    float v = m < p.M ? load_act(p.x, p.act_dtype, m * p.ldx + kk) : 0.0f;
+    if (p.norm_w) v = (v * s_rinv[m]) * p.norm_w[kk];
+    const int pos = (kk / VI::kElems) * VI::kPadded + kk % VI::kElems;
+    if (p.axis == IE_AXIS_K) {
+      xs[m * xstride + pos] = v * p.scale[kk];
+      if (nbuf == 2) xs[(MT + m) * xstride + pos] = v * p.scale[p.K + kk];
+    } else {
+      xs[m * xstride + pos] = v;
+    }
+  }
+  __syncthreads();
+  if constexpr (VI::kInt4) {
+    for (int i = threadIdx.x; i < nbuf * MT * nvec; i += kThreads) {
+      const float* run = xs + (i / nvec) * xstride + (i % nvec) * VI::kPadded;
+      float sum = 0.0f;
+#pragma unroll 8
+      for (int e = 0; e < VI::kElems; ++e) sum += run[e];
+      xsum[i] = sum;
+    }
+    __syncthreads();
+  }
+
+  for (; g < groups; g += g_step) {
+    const int64_t r0 = g * kRows;
+    float acc[kRows][MT];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
+    for (int c0 = 0; c0 < nvec; c0 += 32 * kDecVec) {
+      if (c0 > 0) load_round(g, c0);   // (a group's first round was loaded ahead)
+#pragma unroll
+      for (int u = 0; u < kDecVec; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c >= nvec) continue;
+        float2 part[kRows][MT];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) part[r][m] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            if (b >= nbuf) break;
+            float2 xw[MT][kXw];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              const float4* xr = reinterpret_cast<const float4*>(
+                  xs + (b * MT + m) * xstride + c * VI::kPadded + j * (2 * kXw));
+#pragma unroll
+              for (int h = 0; h < kXw / 2; ++h) {
+                const float4 v = xr[h];
+                xw[m][2 * h] = make_float2(v.x, v.y);
+                xw[m][2 * h + 1] = make_float2(v.z, v.w);
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+              if (nbuf == 2 && (r & 1) != b) continue;
+              const uint32_t w = j == 0 ? wv[u][r].x : j == 1 ? wv[u][r].y
+                               : j == 2 ? wv[u][r].z : wv[u][r].w;
+              dot_word<V, MT>(w, xw, part[r]);
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          if (r0 + r >= p.N) continue;
+          const int buf = (nbuf == 2) ? (r & 1) : 0;
+          if constexpr (V == V_INT4G) {
+            const int64_t gi = ((int64_t)c * VI::kElems / 128) * p.N + (r0 + r);
+            const float sc = __half2float(p.gscale[gi]);
+            const float off = 128.0f + __half2float(p.gzero[gi]);
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+              acc[r][m] += sc * ((part[r][m].x + part[r][m].y) -
+                                 off * xsum[(buf * MT + m) * nvec + c]);
+          } else if constexpr (V == V_INT4SYM) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+              acc[r][m] += (part[r][m].x + part[r][m].y) - 136.0f * xsum[(buf * MT + m) * nvec + c];
+          } else {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[r][m] += part[r][m].x + part[r][m].y;
+          }
+        }
+      }
+    }
+    // the next group's first round goes out before this group's reduction
+    load_round(g + g_step, 0);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float v = acc[r][m];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[r][m] = v;
+      }
+    if (lane == 0) dec_epilogue<V, MT>(p, acc, r0);
+  }
 }
 
 int variant_of(const ie_qweight& w) {
@@ -432,7 +693,57 @@ GemvParams make_params(const ie_qlinear_args& a) {
   p.ldo = a.ldo;
   p.out_dtype = a.out_dtype;
   p.kc = pick_kc(pick_mt(a.m));
+  if (a.epilogue & IE_EPI_RMS_NORM) {
+    p.norm_w = a.norm_weight;
+    p.norm_eps = a.norm_eps;
+  }
   return p;
+}
+
+// Shared memory of the decode kernel (x' of the whole K, padded runs, and the
+// int4 run sums), or 0 when it does not apply: more than two tokens, K not a
+// whole number of code vectors, or x' beyond kDecSmemMax.
+constexpr size_t kDecSmemMax = 160 * 1024;
+size_t dec_smem(const ie_qlinear_args& a) {
+  if (a.m > 2) return 0;
+  const int v = variant_of(a.w);
+  const int elems = (v == V_INT4G || v == V_INT4SYM) ? 32 : 16;
+  const int padded = elems + 4;
+  if (a.w.k % elems) return 0;
+  const int64_t nvec = a.w.k / elems;
+  const int mt = pick_mt(a.m);
+  const int nbuf = (a.w.gate_up && a.w.axis == IE_AXIS_K) ? 2 : 1;
+  size_t f = (size_t)nbuf * mt * nvec * padded;
+  if (elems == 32) f += (size_t)nbuf * mt * nvec;
+  const size_t bytes = f * sizeof(float);
+  return bytes <= kDecSmemMax ? bytes : 0;
+}
+
+template <int V, int MT>
+int launch_dec(const GemvParams& p, size_t smem, cudaStream_t s) {
+  auto kern = gemv_dec_kernel<V, MT>;
+  IE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0, dev = 0, sms = 0;
+  IE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+  IE_CUDA_TRY(cudaGetDevice(&dev));
+  IE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t groups = (p.N + kRows - 1) / kRows;
+  const int64_t need = (groups + kWarps - 1) / kWarps;
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)std::max(per_sm, 1) * sms));
+  kern<<<(unsigned)grid, kThreads, smem, s>>>(p);
+  return launch_status("gemv_dec_kernel");
+}
+
+int dispatch_dec(const ie_qlinear_args& a, size_t smem, cudaStream_t s) {
+  const GemvParams p = make_params(a);
+  const bool two = a.m > 1;
+  switch (variant_of(a.w)) {
+    case V_INT8: return two ? launch_dec<V_INT8, 2>(p, smem, s) : launch_dec<V_INT8, 1>(p, smem, s);
+    case V_INT4SYM:
+      return two ? launch_dec<V_INT4SYM, 2>(p, smem, s) : launch_dec<V_INT4SYM, 1>(p, smem, s);
+    case V_INT4G: return two ? launch_dec<V_INT4G, 2>(p, smem, s) : launch_dec<V_INT4G, 1>(p, smem, s);
+    default: return two ? launch_dec<V_FP8, 2>(p, smem, s) : launch_dec<V_FP8, 1>(p, smem, s);
+  }
 }
 
 int dispatch(const ie_qlinear_args& a, const ReduceCtx* rc, int max_ctas, cudaStream_t s,
@@ -449,6 +760,8 @@ int dispatch(const ie_qlinear_args& a, const ReduceCtx* rc, int max_ctas, cudaSt
 
 }  // namespace
 
+bool gemv_decode_ok(const ie_qlinear_args& a) { return dec_smem(a) > 0; }
+
 int64_t gemv_tiles(const ie_qlinear_args& a) {
   const int mt = pick_mt(a.m);
   return ((a.w.n + kTileRows - 1) / kTileRows) * ((a.m + mt - 1) / mt);
@@ -460,6 +773,10 @@ int gemv_resident_ctas(const ie_qlinear_args& a, int* out) {
 
 int launch_qlinear_gemv(const ie_qlinear_args& a, const ReduceCtx* rc, int max_ctas,
                         cudaStream_t s) {
+  if (!rc) {
+    const size_t smem = dec_smem(a);
+    if (smem) return dispatch_dec(a, smem, s);
+  }
   return dispatch(a, rc, max_ctas, s, nullptr);
 }
 

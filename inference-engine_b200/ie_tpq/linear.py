@@ -115,7 +115,8 @@ def qlinear(x, w: PackedWeight, *, bias=None, residual=None, silu_mul: bool | No
     weight returns ``silu(gate) * up`` of shape ``[M, N/2]``.  ``norm_weight``
     (f32 ``[K]``) folds ``rms_norm(x, norm_weight, norm_eps)`` in front of the
     product (ie/layers/functional.py:6-8); it needs the tensor-core path
-    (``fused_norm_ok``) and raises otherwise.  ``act_quant=IE_ACT_FP8_TOKEN``
+    (``fused_norm_ok``), or the weight-streaming path (``algo=ALGO_GEMV`` or
+    f32 x) for at most two tokens, and raises otherwise.  ``act_quant=IE_ACT_FP8_TOKEN``
     (fp8 weights with per-N or per-tensor scales) quantizes each token of x to
     e4m3 with its own scale and contracts the e4m3 codes on the tensor cores.
     """

@@ -124,12 +124,46 @@ def test_fused_norm_with_the_fused_allreduce_at_world_one():
     assert status_bits() == 0
 
 
+@pytest.mark.parametrize("scheme", ["int4-g128", "int8-k", "fp8-n", "int4-k"])
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_weight_streaming_decode_folds_the_norm(scheme, m, dtype):
+    """The decode GEMV (at most two tokens) stages x for the whole K once per
+    CTA and applies the RMS norm there in f32: rms_norm then the reference's
+    f32 matmul, to f32 accuracy (no f16 rounding of x on this path)."""
+    k, n, eps = 2048, 384, 1e-6
+    q, ref_w = quantize(scheme, o.seeded_weight(k, n, seed=310))
+    p = q.packed()
+    nw = norm_weight(k, 311)
+    xt = torch.from_numpy(activations(m, k, 312 + m)).cuda().to(dtype)
+    res = torch.from_numpy(o.seeded_activations(m, n, seed=313)).cuda().to(dtype)
+    y = qlinear(xt, p, residual=res, norm_weight=torch.from_numpy(nw).cuda(), norm_eps=eps,
+                algo=ALGO_GEMV, out_dtype=torch.float32 if dtype == torch.float32 else None)
+    h = o.rms_norm(xt.float().cpu().numpy(), nw, eps)
+    want = res.float().cpu().numpy() + h @ ref_w
+    tol = 2e-4 if dtype == torch.float32 else RTOL
+    np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=tol, atol=tol / 10)
+
+
+def test_weight_streaming_decode_gate_up_pairs():
+    k, n, m, eps = 1024, 256, 1, 1e-6
+    gq, g_ref = quantize("int4-g128", o.seeded_weight(k, n, seed=320))
+    uq, u_ref = quantize("int4-g128", o.seeded_weight(k, n, seed=321))
+    pair = PackedWeight.pair_gate_up(gq.packed(), uq.packed())
+    nw = norm_weight(k, 322)
+    xt = torch.from_numpy(activations(m, k, seed=323)).cuda()
+    y = qlinear(xt, pair, norm_weight=torch.from_numpy(nw).cuda(), norm_eps=eps,
+                algo=ALGO_GEMV).cpu().numpy()
+    h = o.rms_norm(xt.cpu().numpy(), nw, eps)
+    np.testing.assert_allclose(y, o.silu(h @ g_ref) * (h @ u_ref), rtol=2e-4, atol=2e-5)
+
+
 def test_fused_norm_rejections():
     k, n, m = 1024, 256, 4
     p = W.quantize_grouped(o.seeded_weight(k, n, seed=60)).packed()
     nwt = torch.from_numpy(norm_weight(k, 61)).cuda()
     xt = torch.from_numpy(activations(m, k, seed=62)).cuda().to(torch.bfloat16)
-    # the weight-streaming kernel has no prologue
+    # the weight-streaming kernel folds the norm only for at most two tokens
     with pytest.raises(ValueError):
         qlinear(xt, p, norm_weight=nwt, algo=ALGO_GEMV)
     # f32 activations cannot take the tensor-core path
