@@ -262,15 +262,35 @@ def run_reference(args, rank: int, world: int) -> None:
 PROFILE = REPO / "profiles" / "qgemm_tc_int4g128_b16_ncu_full.md"
 
 
+# committed ncu captures of the gate/up launch at TP=1: (model, scheme, batch) -> summary
+TRAFFIC_PROFILES = {
+    ("llama3-8b", "int4-g128", 16): "qgemm_tc_int4g128_b16_ncu_full.md",
+    ("llama3-70b", "fp8-native", 32): "qgemm_tc_fp8native_llama70b_b32_ncu_full.md",
+}
+
+
+def gate_up_tp1_bytes(scheme: str, batch: int, shape) -> float:
+    """Algorithmic bytes of the TP=1 gate/up launch: packed weights and their
+    tables, the activations and the SiLU*up output."""
+    h, i = shape.hidden, shape.intermediate
+    if scheme == "int4-g128":
+        w = h * 2 * i / 2 + (h // 128) * 2 * i * 4
+    else:   # fp8-native: one byte a weight, one f32 scale per output channel
+        w = h * 2 * i + 2 * i * 4
+    return w + batch * h * 2 + batch * i * 2
+
+
 def measured_traffic(args, kern_bytes: float, shape) -> tuple:
     """DRAM bytes (read + write) of one gate/up launch, from the committed ncu
-    capture of the same kernel at TP=1, batch 16, int4-g128, scaled to this
-    rank's launch by its algorithmic bytes (the traffic grows with the weight
-    rows a rank owns).  None when the workload differs from the capture's."""
-    if args.scheme != "int4-g128" or args.batch != 16 or args.model != "llama3-8b":
+    capture of the same kernel at TP=1 and the same batch and scheme, scaled to
+    this rank's launch by its algorithmic bytes (the traffic grows with the
+    weight rows a rank owns).  None when no capture matches the workload."""
+    name = TRAFFIC_PROFILES.get((args.model, args.scheme, args.batch))
+    if name is None:
         return None, "no capture for this model/scheme/batch"
+    path = PROFILE.parent / name
     try:
-        text = PROFILE.read_text()
+        text = path.read_text()
     except OSError:
         return None, "profile summary missing"
     for line in text.splitlines():
@@ -280,9 +300,8 @@ def measured_traffic(args, kern_bytes: float, shape) -> tuple:
             break
     else:
         return None, "profile summary has no traffic line"
-    h, i = shape.hidden, shape.intermediate
-    tp1 = (h * 2 * i / 2 + (h // 128) * 2 * i * 4) + args.batch * h * 2 + args.batch * i * 2
-    return measured * kern_bytes / tp1, f"ncu dram__bytes_read+write, {PROFILE.name}"
+    tp1 = gate_up_tp1_bytes(args.scheme, args.batch, shape)
+    return measured * kern_bytes / tp1, f"ncu dram__bytes_read+write, {path.name}"
 
 
 def workload_config(args, world: int) -> dict:

@@ -59,3 +59,18 @@ def test_traffic_field_comes_from_the_committed_capture(bench):
     other, why = bench.measured_traffic(SimpleNamespace(scheme="int8", batch=16, model="llama3-8b"),
                                         tp1, shape)
     assert other is None and "no capture" in why
+
+
+def test_traffic_field_for_the_native_fp8_capture(bench):
+    """Llama-3-70B fp8-native at batch 32 reads its gate/up traffic from the
+    native kernel's committed capture: within 2 % of the algorithmic bytes
+    (the extra is the stream-K partials of shared tiles)."""
+    from types import SimpleNamespace
+
+    shape = SimpleNamespace(hidden=8192, intermediate=28672)
+    args = SimpleNamespace(scheme="fp8-native", batch=32, model="llama3-70b")
+    tp1 = bench.gate_up_tp1_bytes("fp8-native", 32, shape)
+    assert tp1 == 472350720
+    traffic, src = bench.measured_traffic(args, tp1, shape)
+    assert src.endswith("qgemm_tc_fp8native_llama70b_b32_ncu_full.md")
+    assert 0 <= (traffic - tp1) / tp1 < 0.02
