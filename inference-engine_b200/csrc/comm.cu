@@ -109,10 +109,9 @@ allreduce_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t n, Reduc
   // the flat array as one token row of n values, tile t = [t * kARTile, ...)
   __shared__ int s_ok;
   const ArOut o{out, nullptr, nullptr, n, 0, 1, n, dtype_of<T>(), false, false};
-  ar_finish_all<kARThreads>(rc, epoch, o, tiles,
-                            [](int64_t t, int64_t& n0, int& rows, int64_t& m0, int& cols) {
+  ar_finish_all<kARThreads, kARTile>(rc, epoch, o, tiles,
+                            [](int64_t t, int64_t& n0, int64_t& m0, int& cols) {
                               n0 = t * kARTile;
-                              rows = kARTile;
                               m0 = 0;
                               cols = 1;
                             },

@@ -238,9 +238,10 @@ struct ArOut {
 // for the owner's values.  kPer elements per thread are loaded together, so a
 // round costs one memory round trip, not one per element.  Returns false when
 // a wait expired (the status word records it); every thread gets the same answer.
-template <int kT>
+template <int kT, int kRows>
 __device__ bool ar_finish_tile(const ReduceCtx& rc, uint32_t epoch, const ArOut& o, int64_t t,
-                               int64_t n0, int rows, int64_t m0, int cols, int* s_ok) {
+                               int64_t n0, int64_t m0, int cols, int* s_ok) {
+  static_assert((kRows & (kRows - 1)) == 0, "tile rows: a power of two");
   const int tid = threadIdx.x;
   const bool two = rc.algo == kArTwoShot;
   const int owner = two ? (int)(t % rc.world) : rc.rank;
@@ -262,41 +263,40 @@ __device__ bool ar_finish_tile(const ReduceCtx& rc, uint32_t epoch, const ArOut&
   const float* mine = landing_slot(rc, rc.rank, epoch);
   const float* src0 = mine + (owns ? 0 : (int64_t)owner * rc.slot_floats);
   constexpr int kPer = 8;
-  const int count = rows * cols;
-  // element e of the tile: row n0 + e % rows, token m0 + e / rows; only e is
-  // kept per element and the rest recomputed, which keeps this tail of the
+  const int count = kRows * cols;
+  // element e of the tile: row n0 + e % kRows, token m0 + e / kRows (shift and
+  // mask, computed once per element); 32-bit locals keep this tail of the
   // fused kernels within their register budget
-  auto at = [&](int e, int64_t ld) { return (m0 + e / rows) * ld + (n0 + e % rows); };
-  auto ok = [&](int e) { return e < count && m0 + e / rows < o.M && n0 + e % rows < o.N; };
   for (int e0 = tid; e0 < count; e0 += kT * kPer) {
-    float v[kPer];
+    int nl[kPer], ml[kPer];
+    bool ok[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int e = e0 + j * kT;
-      v[j] = ok(e) ? __ldcg(src0 + at(e, o.N)) : 0.0f;
+      nl[j] = e & (kRows - 1);
+      ml[j] = e / kRows;
+      ok[j] = e < count && m0 + ml[j] < o.M && n0 + nl[j] < o.N;
     }
+    auto at = [&](int j, int64_t ld) { return (m0 + ml[j]) * ld + (n0 + nl[j]); };
+    float v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) v[j] = ok[j] ? __ldcg(src0 + at(j, o.N)) : 0.0f;
     if (owns) {
       float r[kPer];
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int e = e0 + j * kT;
-        r[j] = (o.has_res && ok(e)) ? ar_load(o.residual, o.dtype, at(e, o.ldr)) : 0.0f;
-      }
+      for (int j = 0; j < kPer; ++j)
+        r[j] = (o.has_res && ok[j]) ? ar_load(o.residual, o.dtype, at(j, o.ldr)) : 0.0f;
       for (int src = 1; src < rc.world; ++src) {
         const float* slot = mine + (int64_t)src * rc.slot_floats;
         float w[kPer];
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int e = e0 + j * kT;
-          w[j] = ok(e) ? __ldcg(slot + at(e, o.N)) : 0.0f;
-        }
+        for (int j = 0; j < kPer; ++j) w[j] = ok[j] ? __ldcg(slot + at(j, o.N)) : 0.0f;
 #pragma unroll
         for (int j = 0; j < kPer; ++j) v[j] += w[j];
       }
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
-        const int e = e0 + j * kT;
-        if (o.has_bias) v[j] += ok(e) ? o.bias[n0 + e % rows] : 0.0f;
+        if (o.has_bias) v[j] += ok[j] ? o.bias[n0 + nl[j]] : 0.0f;
         if (o.has_res) v[j] = r[j] + v[j];
       }
       if (two) {
@@ -304,18 +304,14 @@ __device__ bool ar_finish_tile(const ReduceCtx& rc, uint32_t epoch, const ArOut&
           if (dst == rc.rank) continue;
           float* peer = landing_slot(rc, dst, epoch) + (int64_t)rc.rank * rc.slot_floats;
 #pragma unroll
-          for (int j = 0; j < kPer; ++j) {
-            const int e = e0 + j * kT;
-            if (ok(e)) peer[at(e, o.N)] = v[j];
-          }
+          for (int j = 0; j < kPer; ++j)
+            if (ok[j]) peer[at(j, o.N)] = v[j];
         }
       }
     }
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int e = e0 + j * kT;
-      if (ok(e)) ar_store(o.out, o.dtype, at(e, o.ldo), v[j]);
-    }
+    for (int j = 0; j < kPer; ++j)
+      if (ok[j]) ar_store(o.out, o.dtype, at(j, o.ldo), v[j]);
   }
   __syncthreads();
   if (two && owns && tid < rc.world && tid != rc.rank)
@@ -325,8 +321,9 @@ __device__ bool ar_finish_tile(const ReduceCtx& rc, uint32_t epoch, const ArOut&
 
 // Phase 2 of a fused all-reduce over `tiles` tiles for the whole grid: a
 // two-shot rank finishes the tiles it owns first (they unblock the peers),
-// then copies out the rest.  tile(t, n0, rows, m0, cols) describes tile t.
-template <int kT, typename TileFn>
+// then copies out the rest.  tile(t, n0, m0, cols) describes tile t (kRows
+// rows from n0, cols tokens from m0).
+template <int kT, int kRows, typename TileFn>
 __device__ void ar_finish_all(const ReduceCtx& rc, uint32_t epoch, const ArOut& o, int64_t tiles,
                               TileFn tile, int* s_ok) {
   const bool two = rc.algo == kArTwoShot;
@@ -338,9 +335,9 @@ __device__ void ar_finish_all(const ReduceCtx& rc, uint32_t epoch, const ArOut& 
       const int64_t t = (two && pass == 0) ? rc.rank + i * rc.world : i;
       if (two && pass == 1 && t % rc.world == rc.rank) continue;
       int64_t n0, m0;
-      int rows, cols;
-      tile(t, n0, rows, m0, cols);
-      if (!ar_finish_tile<kT>(rc, epoch, o, t, n0, rows, m0, cols, s_ok)) return;
+      int cols;
+      tile(t, n0, m0, cols);
+      if (!ar_finish_tile<kT, kRows>(rc, epoch, o, t, n0, m0, cols, s_ok)) return;
     }
   }
 }

@@ -382,10 +382,9 @@ gemv_kernel(GemvParams p, ReduceCtx rc, int reduce) {
   __shared__ int s_ok;
   const ArOut o{p.out, p.residual, p.bias, p.ldo, p.ldr, p.M, p.N, p.out_dtype,
                 (p.epilogue & IE_EPI_BIAS) != 0, (p.epilogue & IE_EPI_RESIDUAL) != 0};
-  ar_finish_all<kThreads>(rc, epoch, o, tiles,
-                          [=](int64_t t, int64_t& n0, int& rows, int64_t& m0, int& cols) {
+  ar_finish_all<kThreads, kTileRows>(rc, epoch, o, tiles,
+                          [=](int64_t t, int64_t& n0, int64_t& m0, int& cols) {
                             n0 = (t % row_blocks) * kTileRows;
-                            rows = kTileRows;
                             m0 = (t / row_blocks) * MT;
                             cols = MT;
                           },

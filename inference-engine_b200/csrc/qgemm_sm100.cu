@@ -1733,10 +1733,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     const ArOut o{p.out, p.residual, p.bias, p.ldo, p.ldr, p.M, p.N, p.out_dtype,
                   (p.epilogue & IE_EPI_BIAS) != 0, (p.epilogue & IE_EPI_RESIDUAL) != 0};
     const int n_tiles = p.n_tiles, bn = p.bn;
-    ar_finish_all<kThreads>(rc, epoch, o, (int64_t)p.n_tiles * p.m_tiles,
-                            [=](int64_t t, int64_t& n0, int& rows, int64_t& m0, int& cols) {
+    ar_finish_all<kThreads, kTileN>(rc, epoch, o, (int64_t)p.n_tiles * p.m_tiles,
+                            [=](int64_t t, int64_t& n0, int64_t& m0, int& cols) {
                               n0 = (t % n_tiles) * kTileN;
-                              rows = kTileN;
                               m0 = (t / n_tiles) * bn;
                               cols = bn;
                             },
