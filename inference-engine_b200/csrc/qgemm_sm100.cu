@@ -1873,7 +1873,11 @@ Plan make_plan(const ie_qlinear_args& a, bool allow_split, bool allow_xpre) {
     const double partial =
         s > 1 ? 2.0 * s * (double)M * a.w.n * 4.0 / ((double)sms * pl.w_stage_bytes) : 0.0;
     const double t = waves * (per + kUnitCost + (s > 1 ? kFinalizeCost : 0.0)) + partial;
-    if (t < best - 1e-9) {
+    // Token tiles that can reduce their splits inside a cluster never take
+    // global partials: measured on B200, the Llama-3-8B int4 decode step at 16
+    // tokens runs 3.10 ms with qkv on cluster split-K against 3.29 ms with its
+    // 3-way global split (the ticket round trips sit on every tile's finalize).
+    if ((s == 1 || !cluster_ok) && t < best - 1e-9) {
       best = t;
       pl.splits = s;
       best_cluster = false;
